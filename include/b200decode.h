@@ -1,0 +1,157 @@
+/*
+ * b200decode.h -- C ABI of the B200 (sm_100a) decode kernels: the fused NF4 dequant +
+ * skinny matmul and the split-K flash-decoding GQA attention (partial + log-sum-exp combine).
+ *
+ * Plain C: raw device pointers, sizes, strides in elements, an int status. The library never
+ * allocates device memory: the caller owns every input, output and workspace, and passes the
+ * CUDA stream (a cudaStream_t, written here as void*; NULL is the legacy default stream) that
+ * the work is enqueued on. All calls are asynchronous with respect to the host; a nonzero
+ * status means nothing was launched (argument checks) or the launch itself failed.
+ *
+ * Reference interfaces replaced (paths inside Muhammad-Hamza-cpp/llm-decode-triton-6gb):
+ *   b2d_nf4_gemm            <- NF4Weight.matmul + _nf4_gemm_kernel   profiling/kernels/nf4_gemm.py:94-106, :37-64
+ *   b2d_nf4_dequant         <- bitsandbytes.functional.dequantize_4bit, the stock dequant the
+ *                              reference validates against            profiling/kernels/bench_nf4.py:34
+ *   b2d_gqa_decode_partial  <- _partial_kernel                       profiling/kernels/decode_attention.py:18-55
+ *   b2d_gqa_decode_combine  <- _merge_kernel                         profiling/kernels/decode_attention.py:58-72
+ *   b2d_gqa_decode          <- decode_attention (wrapper)            profiling/kernels/decode_attention.py:75-91
+ *   b2d_nf4_quantize,
+ *   b2d_nf4_double_quant    <- the bitsandbytes quantiser that produced the checkpoint the
+ *                              reference loads (Params4bit / quantize_4bit, profiling/common.py:37-42);
+ *                              used to build models on the device
+ */
+#ifndef B200DECODE_H_
+#define B200DECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+enum {
+  B2D_OK = 0,
+  B2D_ERR_ARG = 1,        /* null pointer where one is required, negative size */
+  B2D_ERR_SHAPE = 2,      /* unsupported shape (e.g. N % 16, K % 64, head_dim, group size) */
+  B2D_ERR_DTYPE = 3,      /* dtype code not supported by this entry point */
+  B2D_ERR_ALIGN = 4,      /* pointer or leading dimension breaks the vector-load alignment */
+  B2D_ERR_WORKSPACE = 5,  /* workspace missing or smaller than the *_workspace_bytes query */
+  B2D_ERR_LAUNCH = 6,     /* the CUDA launch reported an error (message: b2d_last_cuda_error) */
+  B2D_ERR_DEVICE = 7      /* no CUDA device, or not a compute capability 10.x device */
+};
+
+/* dtype codes for activations / outputs */
+enum { B2D_F16 = 0, B2D_BF16 = 1, B2D_F32 = 2 };
+
+const char* b2d_strerror(int status);
+/* Text of the last CUDA error seen by a launch in this thread ("" if none). */
+const char* b2d_last_cuda_error(void);
+/* ABI version: (major << 16) | minor. */
+int b2d_version(void);
+
+/* ================================================================ NF4 storage format
+ * A weight W[N,K] in bitsandbytes NF4: flattened row-major, 64 weights per block, two 4-bit
+ * codes per byte with the EVEN element in the HIGH nibble (nf4_gemm.py:4,55-56).
+ *   packed     uint8, row r starts at packed + r*ld_packed (bytes); ld_packed >= K/2
+ *   absmax     per-block scale: fp32 if nested == 0, uint8 index into code2 if nested != 0;
+ *              row r's blocks start at absmax + r*ld_absmax (elements)
+ *   code2, absmax2, offset   double quantisation (nested != 0):
+ *              scale = fp32(fp32(code2[q] * absmax2[gblk / 256]) + offset)  (nf4_gemm.py:50-51)
+ *              where gblk = gblk_base + r*gblk_row_stride + k/64 is the block's index in the
+ *              FULL tensor (so a tensor-parallel shard indexes absmax2 exactly as the whole)
+ *   code       16 fp32 codebook values (quant_state.code)
+ * Unsharded tensor: ld_packed = K/2, ld_absmax = gblk_row_stride = K/64, gblk_base = 0.
+ * ================================================================================== */
+
+/* out[r, k] = round_dtype(fp32(code[nib] * scale)) for r < n_rows, k < k_cols.
+ * Bit-exact with bitsandbytes.functional.dequantize_4bit. out is row-major with ld_out. */
+int b2d_nf4_dequant(const uint8_t* packed, int64_t ld_packed,
+                    const void* absmax, int64_t ld_absmax, int nested,
+                    const float* code2, const float* absmax2, float offset,
+                    int64_t gblk_base, int64_t gblk_row_stride, const float* code,
+                    void* out, int64_t ld_out, int64_t n_rows, int64_t k_cols, int dtype,
+                    void* stream);
+
+/* Scratch bytes b2d_nf4_gemm needs for (M, N, K) on the current device. Zero-fill a new
+ * workspace once; every launch leaves its counters at zero again, so one workspace can serve
+ * any sequence of calls on one stream (calls that may overlap need separate workspaces). */
+size_t b2d_nf4_gemm_workspace_bytes(int M, int N, int K);
+
+/* y[m, n] = sum_k x[m, k] * W[n, k] for m < M, fp32 accumulation.
+ * x: [M, K] row-major with ldx (elements, multiple of 8, 16-byte aligned base), dtype F16/BF16.
+ * y: [M, N] row-major with ldy, y_dtype = dtype or F32.
+ * Constraints: 1 <= M <= 64, N % 16 == 0, K % 64 == 0 (the reference needs N%64, K%256).
+ * Tensor-core path (mma.sync m16n8k16, fp32 accumulate) over a dequant look-up table. */
+int b2d_nf4_gemm(const void* x, int64_t ldx,
+                 const uint8_t* packed, int64_t ld_packed,
+                 const void* absmax, int64_t ld_absmax, int nested,
+                 const float* code2, const float* absmax2, float offset,
+                 int64_t gblk_base, int64_t gblk_row_stride, const float* code,
+                 void* y, int64_t ldy, int M, int N, int K, int dtype, int y_dtype,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* CUDA-core variant (fp32 FMAs, warp-shuffle reductions, no tensor cores) of b2d_nf4_gemm for
+ * 1 <= M <= 8: same arguments and constraints, no workspace. Kept as the measured comparison
+ * point for the tensor-core path. */
+int b2d_nf4_gemv_simt(const void* x, int64_t ldx,
+                      const uint8_t* packed, int64_t ld_packed,
+                      const void* absmax, int64_t ld_absmax, int nested,
+                      const float* code2, const float* absmax2, float offset,
+                      int64_t gblk_base, int64_t gblk_row_stride, const float* code,
+                      void* y, int64_t ldy, int M, int N, int K, int dtype, int y_dtype,
+                      void* stream);
+
+/* Blockwise NF4 quantisation of n (multiple of 64) contiguous values of dtype F32/F16/BF16:
+ * absmax[b] = max |w| over block b; code index = nearest code to fp32(w * fp32(1/absmax)),
+ * ties to the lower code; packed[i] = idx[2i] << 4 | idx[2i+1]. */
+int b2d_nf4_quantize(const void* w, int64_t n, int dtype, const float* code,
+                     uint8_t* packed, float* absmax, void* stream);
+
+/* Double quantisation of n_blocks fp32 scales: offset = fixed-order float64 mean, rounded to
+ * fp32 (written to *offset_out, a device float); per group of 256: absmax2 = max |a - offset|,
+ * q = nearest code2 entry to fp32((a - offset) * fp32(1/absmax2)). code2 is ascending. */
+int b2d_nf4_double_quant(const float* absmax, int64_t n_blocks, const float* code2,
+                         uint8_t* qabsmax, float* absmax2, float* offset_out, void* stream);
+
+/* ================================================================ GQA decode attention
+ * One query token per sequence. q: [B, H, 1, D] (strides sq_b, sq_h), k/v: [B, KVH, S, D]
+ * (strides s*_b, s*_h, s*_s), out: [B, 1, H, D] (strides so_b, so_h). Last dim contiguous,
+ * strides in elements. Query head h reads KV head h / (H / KVH). seqlens: int32 [B] valid
+ * keys per sequence (NULL = all S). Keys [split*chunk, (split+1)*chunk) form one split.
+ * D in {64, 128}; G = H / KVH in 1..16; dtype F16 or BF16 for q, k, v; out_dtype = dtype or F32.
+ * Workspace (fp32): acc [B, H, nsplit, D] followed by ml [B, H, nsplit, 2].
+ * ================================================================================== */
+
+/* Split count the library picks for (B, KVH, S) on the current device (chunk = ceil(S/nsplit)
+ * rounded up to a multiple of 32 keys). */
+int b2d_gqa_default_splits(int B, int KVH, int S);
+size_t b2d_gqa_workspace_bytes(int B, int H, int nsplit, int D);
+
+int b2d_gqa_decode_partial(const void* q, int64_t sq_b, int64_t sq_h,
+                           const void* k, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                           const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                           const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                           float scale, int nsplit, int chunk, int dtype,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+int b2d_gqa_decode_combine(const int32_t* seqlens, int B, int H, int S, int D,
+                           int nsplit, int chunk, int out_dtype,
+                           const void* workspace, size_t workspace_bytes,
+                           void* out, int64_t so_b, int64_t so_h, void* stream);
+
+/* partial + combine in one call (the combine is launched with programmatic dependent launch so
+ * its launch overlaps the partial kernel's tail). nsplit <= 0 or chunk <= 0 picks defaults. */
+int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h,
+                   const void* k, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                   const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                   const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                   float scale, int nsplit, int chunk, int dtype,
+                   void* workspace, size_t workspace_bytes,
+                   void* out, int64_t so_b, int64_t so_h, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200DECODE_H_ */

@@ -1,0 +1,110 @@
+// Shared helpers for the sm_100a decode kernels: dtype traits, tensor-core fragments,
+// device-property cache and launch-status plumbing for the C ABI in include/b200decode.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "b200decode.h"
+
+namespace b2d {
+
+// ------------------------------------------------------------------ status helpers
+void set_cuda_error(cudaError_t e);
+int launch_status();                      // cudaGetLastError -> B2D_OK / B2D_ERR_LAUNCH
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0;
+  int l2_bytes = 0;
+};
+// Properties of the current device (queried once per device). Returns B2D_OK or B2D_ERR_DEVICE.
+int device_info(DeviceInfo* out);
+
+// ------------------------------------------------------------------ dtype traits
+template <typename T> struct Dt;
+template <> struct Dt<__half> {
+  static __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f32(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ uint16_t bits_rn(float v) { return __half_as_ushort(__float2half_rn(v)); }
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Dt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f32(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ uint16_t bits_rn(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <> struct Dt<float> {
+  static __device__ __forceinline__ float to_f32(float v) { return v; }
+  static __device__ __forceinline__ float from_f32(float v) { return v; }
+};
+
+// ------------------------------------------------------------------ tensor-core fragments
+// D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate. Fragment ownership (lane = 4*g + t):
+//   a0: (row g,   k 2t..2t+1)   a1: (row g+8, k 2t..2t+1)
+//   a2: (row g,   k 2t+8..+9)   a3: (row g+8, k 2t+8..+9)
+//   b0: (k 2t..2t+1, col g)     b1: (k 2t+8..+9, col g)
+//   c0: (row g, col 2t)  c1: (row g, col 2t+1)  c2: (row g+8, col 2t)  c3: (row g+8, col 2t+1)
+template <typename T> struct Mma;
+template <> struct Mma<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+};
+template <> struct Mma<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+};
+
+// ------------------------------------------------------------------ memory helpers
+// Streaming 8/16-byte loads of data read exactly once (weights, KV cache): skip L1 allocation.
+__device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+// Read-only loads that may hit L1 (activations reused by many warps).
+__device__ __forceinline__ uint4 ldg_u4(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return __byte_perm(w, 0u, 0x4440u + i); }
+
+// Programmatic dependent launch: let the next kernel in the stream start its prologue early /
+// wait until the previous kernel's memory is visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace b2d

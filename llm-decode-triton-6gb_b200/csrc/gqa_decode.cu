@@ -1,0 +1,444 @@
+// Split-K flash-decoding grouped-query attention for sm_100a (one query token per sequence).
+//
+// Replaces the reference's _partial_kernel / _merge_kernel / decode_attention
+// (profiling/kernels/decode_attention.py:18-91): every CTA owns one (sequence, KV head, key split)
+// and serves all G = H/KVH query heads of that KV head, so each K/V row is read from HBM once; a
+// second kernel merges the splits with a log-sum-exp combine. Adds per-sequence lengths.
+//
+// Partial kernel, per warp and 16-key tile (m16n8k16, fp32 accumulate):
+//   S = Q K^T   A = Q (16 rows = query heads of the group, rows >= G are zero), B = K^T.
+//               Thread (g,t) loads key rows g and 8+g of the tile, head-dim slice [D/4*t, D/4*t+D/4)
+//               with 16-byte loads; the MMA reduction axis is permuted to match (k-step j uses
+//               d = D/4*t + 4j + {0..3}), and Q is loaded in the same permuted order.
+//   P = exp2(S*scale*log2e - m)   online softmax per head, max over the tile's 16 keys by a
+//               quad shuffle; the S accumulator layout is the A-operand layout of the next MMA.
+//   O += P V    B = V: thread (g,t) loads value rows 2t, 2t+1, 8+2t, 9+2t over the head-dim slice
+//               [D/8*g, D/8*g+D/8) and pairs rows with byte permutes; output column n of n8 tile j
+//               is d = D/8*(column) + j, so each thread ends up owning O[head][D/4*t .. D/4*t+D/4).
+//   No shared-memory staging for K/V: 16-byte global loads straight into fragment registers, one
+//   tile prefetched ahead. Warps of a CTA take interleaved tiles and merge through shared memory.
+// Workspace per (b, h, split): unnormalised O[D] (fp32) and (m, l) with m in the log2 domain.
+#include "common.cuh"
+
+namespace b2d {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  const void* q; int64_t sq_b, sq_h;
+  const void* k; int64_t sk_b, sk_h, sk_s;
+  const void* v; int64_t sv_b, sv_h, sv_s;
+  const int32_t* seqlens;
+  int B, H, KVH, S, G;
+  float scale_log2;
+  int nsplit, chunk;
+  float* acc;   // [B*H*nsplit][D]
+  float* ml;    // [B*H*nsplit][2]
+  void* out; int64_t so_b, so_h;
+};
+
+__device__ __forceinline__ int seqlen_of(const AttnArgs& a, int b) {
+  if (!a.seqlens) return a.S;
+  int n = a.seqlens[b];
+  return n < 0 ? 0 : (n > a.S ? a.S : n);
+}
+
+template <typename T, int D>
+struct KvTile {
+  uint4 k[2][D / 32];   // key rows g, 8+g; head-dim slice D/4 wide
+  uint4 v[4][D / 64];   // value rows 2t, 2t+1, 8+2t, 9+2t; head-dim slice D/8 wide
+};
+
+template <typename T, int D>
+__device__ __forceinline__ void load_tile(KvTile<T, D>& kt, const T* kbase, const T* vbase, int64_t sk_s,
+                                          int64_t sv_s, int tok0, int tend, int g, int tq) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int tok = tok0 + r * 8 + g;
+    const T* p = kbase + static_cast<int64_t>(tok) * sk_s + (D / 4) * tq;
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i)
+      kt.k[r][i] = tok < tend ? ldg_stream_u4(p + 8 * i) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int tok = tok0 + (r >> 1) * 8 + 2 * tq + (r & 1);
+    const T* p = vbase + static_cast<int64_t>(tok) * sv_s + (D / 8) * g;
+#pragma unroll
+    for (int i = 0; i < D / 64; ++i)
+      kt.v[r][i] = tok < tend ? ldg_stream_u4(p + 8 * i) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T, int D, bool TWO_HALVES>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const AttnArgs a) {
+  constexpr int KSTEPS = D / 16;   // MMA k-steps over the head dim
+  constexpr int NTILES = D / 8;    // n8 output tiles of O
+  constexpr int ROWS = TWO_HALVES ? 16 : 8;
+  __shared__ float s_o[kAttnWarps][ROWS][D];
+  __shared__ float s_m[kAttnWarps][ROWS], s_l[kAttnWarps][ROWS];
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int len = seqlen_of(a, b);
+  const int t_begin = split * a.chunk;
+  if (t_begin >= len) return;   // this split holds no keys; the combine skips it
+  const int t_end = min(t_begin + a.chunk, len);
+
+  // ---- Q fragments (rows = heads of this KV group), permuted head-dim order
+  const T* qb = static_cast<const T*>(a.q) + b * a.sq_b;
+  uint32_t qa[KSTEPS][4];
+  {
+    const int h0 = kvh * a.G + g, h1 = kvh * a.G + g + 8;
+    const T* q0 = qb + static_cast<int64_t>(h0) * a.sq_h + (D / 4) * tq;
+    const T* q1 = qb + static_cast<int64_t>(h1) * a.sq_h + (D / 4) * tq;
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) {
+      const uint4 u0 = g < a.G ? __ldg(reinterpret_cast<const uint4*>(q0) + i) : make_uint4(0, 0, 0, 0);
+      uint4 u1 = make_uint4(0, 0, 0, 0);
+      if (TWO_HALVES && g + 8 < a.G) u1 = __ldg(reinterpret_cast<const uint4*>(q1) + i);
+      // k-steps 2i and 2i+1 take the 8 halves of this uint4: a0/a2 = (d, d+1)/(d+2, d+3)
+      qa[2 * i][0] = u0.x; qa[2 * i][2] = u0.y; qa[2 * i + 1][0] = u0.z; qa[2 * i + 1][2] = u0.w;
+      qa[2 * i][1] = u1.x; qa[2 * i][3] = u1.y; qa[2 * i + 1][1] = u1.z; qa[2 * i + 1][3] = u1.w;
+    }
+  }
+
+  const T* kbase = static_cast<const T*>(a.k) + b * a.sk_b + kvh * a.sk_h;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.sv_b + kvh * a.sv_h;
+
+  float o[NTILES][4];
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};   // rows g, g+8 (log2 domain)
+  float l_run[2] = {0.f, 0.f};               // per-thread partial sums over its keys
+
+  const int ntiles = (t_end - t_begin + 15) / 16;
+  KvTile<T, D> cur, nxt;
+  int tile = warp;
+  if (tile < ntiles) load_tile<T, D>(cur, kbase, vbase, a.sk_s, a.sv_s, t_begin + 16 * tile, t_end, g, tq);
+  for (; tile < ntiles; tile += kAttnWarps) {
+    const int tok0 = t_begin + 16 * tile;
+    if (tile + kAttnWarps < ntiles)
+      load_tile<T, D>(nxt, kbase, vbase, a.sk_s, a.sv_s, tok0 + 16 * kAttnWarps, t_end, g, tq);
+
+    // S for keys tok0+[0,8) (s0) and tok0+[8,16) (s1)
+    float s[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      s[h][0] = s[h][1] = s[h][2] = s[h][3] = 0.f;
+#pragma unroll
+      for (int j = 0; j < KSTEPS; ++j) {
+        const uint32_t* kw = reinterpret_cast<const uint32_t*>(&cur.k[h][0]);
+        Mma<T>::run(s[h], qa[j][0], qa[j][1], qa[j][2], qa[j][3], kw[2 * j], kw[2 * j + 1]);
+      }
+    }
+    // scale, mask, online softmax
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int tok = tok0 + h * 8 + 2 * tq + (c & 1);
+        s[h][c] = tok < t_end ? s[h][c] * a.scale_log2 : -INFINITY;
+        tmax[c >> 1] = fmaxf(tmax[c >> 1], s[h][c]);
+      }
+    }
+    float alpha[2], msafe[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
+      const float m_new = fmaxf(m_run[r], tmax[r]);
+      msafe[r] = m_new == -INFINITY ? 0.f : m_new;
+      alpha[r] = exp2f(m_run[r] - msafe[r]);
+      m_run[r] = m_new;
+    }
+    uint32_t pa[4];
+    {
+      float p[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) p[h][c] = exp2f(s[h][c] - msafe[c >> 1]);
+      l_run[0] = l_run[0] * alpha[0] + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
+      l_run[1] = l_run[1] * alpha[1] + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+      pa[0] = Dt<T>::pack2(p[0][0], p[0][1]);   // row g,   keys 2t, 2t+1
+      pa[1] = Dt<T>::pack2(p[0][2], p[0][3]);   // row g+8
+      pa[2] = Dt<T>::pack2(p[1][0], p[1][1]);   // row g,   keys 8+2t, 9+2t
+      pa[3] = Dt<T>::pack2(p[1][2], p[1][3]);
+    }
+    // O = alpha*O + P V
+    const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&cur.v[0][0]);
+    const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&cur.v[1][0]);
+    const uint32_t* v2 = reinterpret_cast<const uint32_t*>(&cur.v[2][0]);
+    const uint32_t* v3 = reinterpret_cast<const uint32_t*>(&cur.v[3][0]);
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n) {
+      o[n][0] *= alpha[0]; o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
+      const uint32_t sel = (n & 1) ? 0x7632u : 0x5410u;
+      const uint32_t b0 = __byte_perm(v0[n >> 1], v1[n >> 1], sel);
+      const uint32_t b1 = __byte_perm(v2[n >> 1], v3[n >> 1], sel);
+      Mma<T>::run(o[n], pa[0], pa[1], pa[2], pa[3], b0, b1);
+    }
+    if (tile + kAttnWarps < ntiles) cur = nxt;
+  }
+
+  // ---- per-warp results -> shared memory (rows g, g+8; thread owns d in [D/4*t, D/4*t + D/4))
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+#pragma unroll
+  for (int r = 0; r < (TWO_HALVES ? 2 : 1); ++r) {
+    const int row = g + 8 * r;
+    if (tq == 0) {
+      s_m[warp][row] = m_run[r];
+      s_l[warp][row] = l_run[r];
+    }
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n) {
+      s_o[warp][row][(D / 4) * tq + n] = o[n][2 * r];
+      s_o[warp][row][(D / 4) * tq + D / 8 + n] = o[n][2 * r + 1];
+    }
+  }
+  __syncthreads();
+
+  // ---- merge the warps and write this split's partial
+  const int nrows = min(a.G, ROWS);
+  const int64_t slot0 = (static_cast<int64_t>(b) * a.H + kvh * a.G) * a.nsplit + split;
+  for (int idx = threadIdx.x; idx < nrows * D; idx += kAttnWarps * 32) {
+    const int row = idx / D, d = idx - row * D;
+    float mx = s_m[0][row];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_m[w][row]);
+    float acc = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float e = s_m[w][row] == -INFINITY ? 0.f : exp2f(s_m[w][row] - mx);
+      acc += e * s_o[w][row][d];
+      l += e * s_l[w][row];
+    }
+    const int64_t slot = slot0 + static_cast<int64_t>(row) * a.nsplit;
+    a.acc[slot * D + d] = acc;
+    if (d == 0) {
+      a.ml[slot * 2] = mx;
+      a.ml[slot * 2 + 1] = l;
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// One CTA per (b, h), one thread per head-dim element. OT: output dtype.
+template <typename OT, int D>
+__global__ void __launch_bounds__(D) gqa_combine_kernel(const AttnArgs a) {
+  pdl_wait();   // partial results of the previous kernel are visible after this
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh - b * a.H;
+  const int d = threadIdx.x;
+  const int len = seqlen_of(a, b);
+  const int nvalid = min(a.nsplit, (len + a.chunk - 1) / a.chunk);
+  const int64_t base = static_cast<int64_t>(bh) * a.nsplit;
+  float mx = -INFINITY;
+  for (int i = 0; i < nvalid; ++i) mx = fmaxf(mx, a.ml[(base + i) * 2]);
+  float num = 0.f, den = 0.f;
+  for (int i = 0; i < nvalid; ++i) {
+    const float m = a.ml[(base + i) * 2];
+    const float w = m == -INFINITY ? 0.f : exp2f(m - mx);
+    num += w * a.acc[(base + i) * D + d];
+    den += w * a.ml[(base + i) * 2 + 1];
+  }
+  OT* out = static_cast<OT*>(a.out) + b * a.so_b + h * a.so_h;
+  out[d] = Dt<OT>::from_f32(den > 0.f ? num / den : 0.f);
+}
+
+int check_attn(int B, int H, int KVH, int S, int D, int dtype) {
+  if (B < 0 || H < 0 || KVH < 0 || S < 0) return B2D_ERR_ARG;
+  if (dtype != B2D_F16 && dtype != B2D_BF16) return B2D_ERR_DTYPE;
+  if (D != 64 && D != 128) return B2D_ERR_SHAPE;
+  if (KVH == 0 || H % KVH != 0 || H / KVH > 16) return B2D_ERR_SHAPE;
+  return B2D_OK;
+}
+
+int fill_args(AttnArgs* a, const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b, int64_t sk_h,
+              int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s, const int32_t* seqlens, int B,
+              int H, int KVH, int S, int D, float scale, int nsplit, int chunk, const void* ws, size_t ws_bytes) {
+  if (nsplit <= 0 || chunk <= 0 || chunk % 16 != 0) return B2D_ERR_SHAPE;
+  if (static_cast<int64_t>(nsplit) * chunk < S) return B2D_ERR_SHAPE;
+  if (!ws || ws_bytes < b2d_gqa_workspace_bytes(B, H, nsplit, D)) return B2D_ERR_WORKSPACE;
+  if (!aligned(ws, 16)) return B2D_ERR_ALIGN;
+  *a = AttnArgs{};
+  a->q = q; a->sq_b = sq_b; a->sq_h = sq_h;
+  a->k = k; a->sk_b = sk_b; a->sk_h = sk_h; a->sk_s = sk_s;
+  a->v = v; a->sv_b = sv_b; a->sv_h = sv_h; a->sv_s = sv_s;
+  a->seqlens = seqlens;
+  a->B = B; a->H = H; a->KVH = KVH; a->S = S; a->G = KVH ? H / KVH : 1;
+  a->scale_log2 = scale * kLog2e;
+  a->nsplit = nsplit; a->chunk = chunk;
+  a->acc = static_cast<float*>(const_cast<void*>(ws));
+  a->ml = a->acc + static_cast<size_t>(B) * H * nsplit * D;
+  return B2D_OK;
+}
+
+template <typename T, int D>
+int launch_partial_t(const AttnArgs& a, cudaStream_t s) {
+  dim3 grid(a.nsplit, a.KVH, a.B);
+  if (a.G > 8) gqa_partial_kernel<T, D, true><<<grid, kAttnWarps * 32, 0, s>>>(a);
+  else gqa_partial_kernel<T, D, false><<<grid, kAttnWarps * 32, 0, s>>>(a);
+  return launch_status();
+}
+
+int launch_partial(const AttnArgs& a, int D, int dtype, cudaStream_t s) {
+  if (dtype == B2D_F16) {
+    if (D == 64) return launch_partial_t<__half, 64>(a, s);
+    return launch_partial_t<__half, 128>(a, s);
+  }
+  if (D == 64) return launch_partial_t<__nv_bfloat16, 64>(a, s);
+  return launch_partial_t<__nv_bfloat16, 128>(a, s);
+}
+
+template <typename T, int D>
+int launch_combine_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.B * a.H);
+  cfg.blockDim = dim3(D);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, D>, a);
+  if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
+  return launch_status();
+}
+
+int launch_combine(const AttnArgs& a, int D, int out_dtype, cudaStream_t s, bool pdl) {
+  if (out_dtype == B2D_F16) {
+    if (D == 64) return launch_combine_t<__half, 64>(a, s, pdl);
+    return launch_combine_t<__half, 128>(a, s, pdl);
+  }
+  if (out_dtype == B2D_BF16) {
+    if (D == 64) return launch_combine_t<__nv_bfloat16, 64>(a, s, pdl);
+    return launch_combine_t<__nv_bfloat16, 128>(a, s, pdl);
+  }
+  if (D == 64) return launch_combine_t<float, 64>(a, s, pdl);
+  return launch_combine_t<float, 128>(a, s, pdl);
+}
+
+int check_strides(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                  const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s) {
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16)) return B2D_ERR_ALIGN;
+  if ((sq_b | sq_h | sk_b | sk_h | sk_s | sv_b | sv_h | sv_s) % 8 != 0) return B2D_ERR_ALIGN;
+  return B2D_OK;
+}
+
+}  // namespace
+}  // namespace b2d
+
+using namespace b2d;
+
+extern "C" int b2d_gqa_default_splits(int B, int KVH, int S) {
+  DeviceInfo di;
+  if (device_info(&di) != B2D_OK || B <= 0 || KVH <= 0 || S <= 0) return 1;
+  const int64_t pairs = static_cast<int64_t>(B) * KVH;
+  const int64_t target = static_cast<int64_t>(di.sm_count) * 8;   // ~4 waves at 2 CTAs/SM
+  int64_t ns = (target + pairs - 1) / pairs;
+  const int64_t max_ns = (S + 63) / 64;                          // keep >= 64 keys per split
+  if (ns > max_ns) ns = max_ns;
+  if (ns < 1) ns = 1;
+  // round chunk up to a multiple of 32 keys and recompute the split count
+  int64_t chunk = (S + ns - 1) / ns;
+  chunk = (chunk + 31) / 32 * 32;
+  return static_cast<int>((S + chunk - 1) / chunk);
+}
+
+extern "C" size_t b2d_gqa_workspace_bytes(int B, int H, int nsplit, int D) {
+  if (B <= 0 || H <= 0 || nsplit <= 0 || D <= 0) return 0;
+  return static_cast<size_t>(B) * H * nsplit * (D + 2) * sizeof(float);
+}
+
+static int default_chunk(int S, int nsplit) {
+  int chunk = (S + nsplit - 1) / nsplit;
+  return (chunk + 31) / 32 * 32;
+}
+
+extern "C" int b2d_gqa_decode_partial(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b,
+                                      int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h,
+                                      int64_t sv_s, const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                                      float scale, int nsplit, int chunk, int dtype, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  int st = check_attn(B, H, KVH, S, D, dtype);
+  if (st != B2D_OK) return st;
+  if (B == 0 || H == 0 || S == 0) return B2D_OK;
+  if (!q || !k || !v) return B2D_ERR_ARG;
+  if ((st = check_strides(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s)) != B2D_OK) return st;
+  DeviceInfo di;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  AttnArgs a;
+  if ((st = fill_args(&a, q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
+                      nsplit, chunk, workspace, workspace_bytes)) != B2D_OK)
+    return st;
+  if (nsplit > 65535 || KVH > 65535 || B > 65535) return B2D_ERR_SHAPE;
+  return launch_partial(a, D, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2d_gqa_decode_combine(const int32_t* seqlens, int B, int H, int S, int D, int nsplit, int chunk,
+                                      int out_dtype, const void* workspace, size_t workspace_bytes, void* out,
+                                      int64_t so_b, int64_t so_h, void* stream) {
+  if (B < 0 || H < 0 || S < 0) return B2D_ERR_ARG;
+  if (out_dtype != B2D_F16 && out_dtype != B2D_BF16 && out_dtype != B2D_F32) return B2D_ERR_DTYPE;
+  if (D != 64 && D != 128) return B2D_ERR_SHAPE;
+  if (B == 0 || H == 0) return B2D_OK;
+  if (!out) return B2D_ERR_ARG;
+  int st;
+  DeviceInfo di;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  AttnArgs a;
+  if ((st = fill_args(&a, nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, 0, seqlens, B, H, 1, S, D, 1.f,
+                      nsplit, chunk, workspace, workspace_bytes)) != B2D_OK)
+    return st;
+  a.G = 1;
+  a.out = out; a.so_b = so_b; a.so_h = so_h;
+  return launch_combine(a, D, out_dtype, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b, int64_t sk_h,
+                              int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                              const int32_t* seqlens, int B, int H, int KVH, int S, int D, float scale, int nsplit,
+                              int chunk, int dtype, void* workspace, size_t workspace_bytes, void* out, int64_t so_b,
+                              int64_t so_h, int out_dtype, void* stream) {
+  int st = check_attn(B, H, KVH, S, D, dtype);
+  if (st != B2D_OK) return st;
+  if (out_dtype != dtype && out_dtype != B2D_F32) return B2D_ERR_DTYPE;
+  if (B == 0 || H == 0) return B2D_OK;
+  if (!out) return B2D_ERR_ARG;
+  if (S == 0) return B2D_ERR_SHAPE;   // nothing to attend to
+  if (!q || !k || !v) return B2D_ERR_ARG;
+  if ((st = check_strides(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s)) != B2D_OK) return st;
+  DeviceInfo di;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  if (nsplit <= 0 && chunk <= 0) {
+    nsplit = b2d_gqa_default_splits(B, KVH, S);
+    chunk = default_chunk(S, nsplit);
+    nsplit = (S + chunk - 1) / chunk;
+  } else if (chunk <= 0) {
+    chunk = default_chunk(S, nsplit);
+  } else if (nsplit <= 0) {
+    nsplit = (S + chunk - 1) / chunk;
+  }
+  AttnArgs a;
+  if ((st = fill_args(&a, q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
+                      nsplit, chunk, workspace, workspace_bytes)) != B2D_OK)
+    return st;
+  if (nsplit > 65535 || KVH > 65535 || B > 65535) return B2D_ERR_SHAPE;
+  a.out = out; a.so_b = so_b; a.so_h = so_h;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = launch_partial(a, D, dtype, s)) != B2D_OK) return st;
+  return launch_combine(a, D, out_dtype, s, true);
+}

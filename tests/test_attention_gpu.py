@@ -1,0 +1,140 @@
+"""GPU parity of the split-K GQA decode attention (through the C ABI) against the CPU oracle.
+
+Bar: max|out - ref| <= 2e-3 * rms(ref) for an fp32 output (the reference formula is fp32 SDPA on
+repeated KV heads, ``bench_attention.py:40-41``), plus one output unit for fp16/bf16 outputs.
+"""
+import glob
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from b200kernels import _lib
+from b200kernels.decode_attention import decode_attention, plan_splits
+from oracle import attn_ref
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = 2e-3
+
+
+def rand_case(B, H, KVH, S, D, dtype=torch.float16, seed=0, lens=None):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, 1, D, generator=g).to(dtype)
+    k = torch.randn(B, KVH, S, D, generator=g).to(dtype)
+    v = torch.randn(B, KVH, S, D, generator=g).to(dtype)
+    sl = None if lens is None else torch.tensor(lens, dtype=torch.int32)
+    return q, k, v, sl
+
+
+def check(out, ref, tol=TOL, unit=None):
+    out = out.double().cpu().numpy().reshape(ref.shape)
+    rms = np.sqrt((ref ** 2).mean())
+    bound = tol * rms + (0 if unit is None else np.abs(ref) * unit)
+    err = np.abs(out - ref)
+    assert np.all(err <= bound), f"max err {err.max():.3e} rms {rms:.3e}"
+
+
+def run(q, k, v, sl, out_dtype=torch.float32, **kw):
+    return decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), q.shape[-1] ** -0.5,
+                            seqlens=None if sl is None else sl.to(DEV), out_dtype=out_dtype, **kw)
+
+
+def oracle(q, k, v, sl):
+    return attn_ref.gqa_decode_ref(q.float().numpy(), k.float().numpy(), v.float().numpy(), q.shape[-1] ** -0.5,
+                                   None if sl is None else sl.numpy())
+
+
+def test_config_shape_ragged_lengths():
+    """B=8, H=32, KVH=8, S=2048, D=128, fp16, lengths uniform in [512, 2048]."""
+    g = torch.Generator().manual_seed(1)
+    lens = torch.randint(512, 2049, (8,), generator=g).tolist()
+    q, k, v, sl = rand_case(8, 32, 8, 2048, 128, seed=2, lens=lens)
+    ref = oracle(q, k, v, sl)
+    check(run(q, k, v, sl), ref)
+    check(run(q, k, v, sl, out_dtype=torch.float16), ref, unit=2.0 ** -10)
+
+
+@pytest.mark.parametrize("B,H,KVH,S,D", [(1, 32, 8, 1, 128), (2, 32, 8, 15, 128), (3, 32, 8, 17, 128),
+                                         (1, 8, 8, 300, 64), (2, 16, 2, 129, 64), (1, 16, 1, 777, 128),
+                                         (2, 4, 1, 33, 128), (1, 12, 4, 95, 128)])
+def test_odd_shapes_full_length(B, H, KVH, S, D):
+    q, k, v, sl = rand_case(B, H, KVH, S, D, seed=S)
+    check(run(q, k, v, sl), oracle(q, k, v, sl))
+
+
+def test_ragged_with_empty_and_single_key():
+    q, k, v, sl = rand_case(4, 32, 8, 200, 128, seed=9, lens=[0, 1, 200, 63])
+    out = run(q, k, v, sl)
+    ref = oracle(q, k, v, sl)
+    assert torch.all(out[0] == 0)
+    check(out[1:], ref[1:])
+
+
+@pytest.mark.parametrize("chunk", [16, 64, 100, 2048])
+def test_explicit_chunks(chunk):
+    q, k, v, sl = rand_case(2, 32, 8, 1000, 128, seed=4, lens=[1000, 517])
+    check(run(q, k, v, sl, chunk=chunk), oracle(q, k, v, sl))
+
+
+def test_bf16():
+    q, k, v, sl = rand_case(4, 32, 8, 512, 128, dtype=torch.bfloat16, seed=5, lens=[512, 100, 333, 1])
+    ref = oracle(q, k, v, sl)
+    check(run(q, k, v, sl), ref)
+    check(run(q, k, v, sl, out_dtype=torch.bfloat16), ref, unit=2.0 ** -7)
+
+
+def test_strided_cache_views():
+    """K/V as views into a larger preallocated cache (HF static-cache style), q from a [B,1,H,D] buffer."""
+    B, H, KVH, S, D, SMAX = 2, 32, 8, 300, 128, 512
+    g = torch.Generator().manual_seed(6)
+    kc = torch.randn(B, KVH, SMAX, D, generator=g).half()
+    vc = torch.randn(B, KVH, SMAX, D, generator=g).half()
+    qb = torch.randn(B, 1, H, D, generator=g).half()
+    q = qb.transpose(1, 2)                        # [B, H, 1, D], strides (H*D, D, .., 1)
+    k, v = kc[:, :, :S], vc[:, :, :S]
+    out = decode_attention(q.to(DEV), kc.to(DEV)[:, :, :S], vc.to(DEV)[:, :, :S], D ** -0.5,
+                           out_dtype=torch.float32)
+    check(out, oracle(q.contiguous(), k.contiguous(), v.contiguous(), None))
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(str(GOLDEN / "attn_ref_*.npz"))))
+def test_against_reference_stock_golden(path):
+    d = dict(np.load(path))
+    q, k, v = (torch.from_numpy(d[n]).to(DEV) for n in ("q", "k", "v"))
+    sl = torch.from_numpy(d["seqlens"]).to(DEV)
+    out = decode_attention(q, k, v, float(d["scale"]), seqlens=sl, out_dtype=torch.float32)
+    check(out, d["out"].astype(np.float64))
+
+
+def test_matches_torch_sdpa_on_device():
+    """The reference's stock path on the same GPU: repeat_kv + SDPA (fp32), no mask."""
+    import torch.nn.functional as F
+    from transformers.integrations.sdpa_attention import repeat_kv
+    q, k, v, _ = rand_case(4, 32, 8, 1024, 128, seed=7)
+    q, k, v = q.to(DEV), k.to(DEV), v.to(DEV)
+    ref = F.scaled_dot_product_attention(q.float(), repeat_kv(k, 4).float(), repeat_kv(v, 4).float(),
+                                         scale=128 ** -0.5).transpose(1, 2)
+    out = decode_attention(q, k, v, 128 ** -0.5, out_dtype=torch.float32)
+    check(out, ref.double().cpu().numpy())
+
+
+def test_split_plan_and_workspace():
+    ns, chunk = plan_splits(8, 8, 2048)
+    assert ns * chunk >= 2048 and chunk % 32 == 0
+    assert ns == -(-2048 // chunk)
+    lib = _lib.load()
+    assert lib.b2d_gqa_workspace_bytes(8, 32, ns, 128) == 8 * 32 * ns * 130 * 4
+
+
+def test_rejects_bad_inputs():
+    q, k, v, _ = rand_case(1, 32, 8, 16, 128)
+    with pytest.raises(TypeError):
+        decode_attention(q.to(DEV), k.to(DEV).float(), v.to(DEV), 0.1)
+    with pytest.raises(ValueError):
+        decode_attention(torch.randn(1, 32, 2, 128, device=DEV).half(), k.to(DEV), v.to(DEV), 0.1)
+    with pytest.raises(_lib.B2DError):
+        decode_attention(torch.randn(1, 32, 1, 96, device=DEV).half(), torch.randn(1, 8, 16, 96, device=DEV).half(),
+                         torch.randn(1, 8, 16, 96, device=DEV).half(), 0.1)
