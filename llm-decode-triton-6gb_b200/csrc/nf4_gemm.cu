@@ -6,17 +6,19 @@
 // code2[q]*absmax2[blk/256]+offset (nf4_gemm.py:48-56); fp32 accumulation.
 //
 // Design (HBM-bound: ~0.52 B of weight state per weight, 2*M flops per weight):
-//  * Persistent grid, one CTA per SM. The work is the list of (row group, 64-weight block) pairs in
-//    row-group-major order; every CTA gets an equal contiguous slice and every warp an equal
-//    contiguous sub-slice, so all SMs stream the same number of bytes for any (N, K). A row group
-//    split between warps is summed in shared memory, one split between CTAs through a small global
-//    workspace; the CTA that finishes a shared group last (atomic counter) adds the partials in
-//    CTA order, so results are deterministic.
+//  * Persistent grid, one CTA per SM. The work is the list of (row group, chunk of CB 64-weight
+//    blocks) units in row-group-major order; every CTA gets an equal contiguous slice and every warp
+//    an equal contiguous sub-slice, so all SMs stream the same number of bytes for any (N, K). A row
+//    group split between warps is summed in shared memory, one split between CTAs through a small
+//    global workspace; the CTA that finishes a shared group last (acquire-release atomic counter)
+//    adds the partials in CTA order, so results are deterministic.
 //  * Weights go global -> registers with 8-byte streaming loads (no shared-memory staging: the
-//    shared-memory pipe is reserved for the dequant table), prefetched P pairs ahead.
+//    shared-memory pipe is reserved for the dequant table), double-buffered one unit ahead; the
+//    first unit's loads are issued before the table is built.
 //  * Dequant: a 256-entry table maps one packed byte to the pair (code[hi], code[lo]) in the
-//    activation dtype, i.e. directly to one tensor-core A-fragment register. The table is
-//    replicated once per lane (entry e, lane l at word 32e+l), so lookups never bank-conflict.
+//    activation dtype, i.e. directly to one tensor-core A-fragment register. Entry e, lane l lives
+//    at byte 256*e + 4*l, so lookups never bank-conflict and one byte permute of the packed word
+//    with 4*lane produces the address.
 //  * The per-block scale is factored out of the dot product: the four m16n8k16 MMAs of one block
 //    accumulate sum_k x_k*code[n_k] from zero, and the fp32 block scale multiplies that partial
 //    into the running fp32 accumulator (one FMA per output element per block).
@@ -29,9 +31,9 @@ namespace b2d {
 
 namespace {
 
-constexpr int kLutWords = 256 * 32;      // 256 byte values x 32 per-lane copies
-constexpr int kGemmWarps = 8;
-constexpr int kGemmThreads = kGemmWarps * 32;
+constexpr int kLutEntryBytes = 256;                 // 32 lanes x 4 B used; stride chosen for the permute
+constexpr int kLutBytes = 256 * kLutEntryBytes;     // 64 KB
+constexpr int kCode2Bytes = 256 * 4;
 
 struct Nf4View {
   const uint8_t* packed;
@@ -53,93 +55,124 @@ struct GemmArgs {
   void* y;
   int64_t ldy;
   int M, N, K;
-  int kb;            // K / 64
-  int64_t groups;    // N / (16 * RT)
-  int64_t total;     // groups * kb
+  int upg;           // units (chunks of CB blocks) per row group = K / (64 * CB)
+  int groups;        // N / (16 * RT)
+  int total;         // groups * upg
   float* partials;   // [grid][2][E]
   int* counters;     // [groups]
 };
 
-template <int RT, int NT>
-struct Stage {
-  uint2 w[RT][2];        // rows g and g+8 of each 16-row tile: this thread's 8 bytes of the block
-  uint32_t sraw[RT][2];  // fp32 bits of absmax, or the uint8 double-quant index
-  float a2[RT][2];       // absmax2 of the block's group (double quant)
-  uint4 xv[NT][2];       // 16 activations of token 8*nt+g for this thread's k offsets
+template <int RT, int CB>
+struct WBuf {
+  uint2 w[RT][2][CB];    // rows g, g+8 of each 16-row tile; this thread's 8 bytes of each block
 };
 
-template <typename T, int RT, int NT, bool NESTED>
-__device__ __forceinline__ void load_stage(Stage<RT, NT>& st, const GemmArgs& a, int64_t grp, int blk,
-                                           int g, int tq) {
-  const T* x = static_cast<const T*>(a.x);
+template <int RT, int CB>
+__device__ __forceinline__ void load_w(WBuf<RT, CB>& b, const GemmArgs& a, int grp, int unit, int g, int tq) {
 #pragma unroll
   for (int rt = 0; rt < RT; ++rt) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int64_t row = grp * (16 * RT) + rt * 16 + h * 8 + g;
-      st.w[rt][h] = ldg_stream_u2(a.w.packed + row * a.w.ld_packed + blk * 32 + tq * 8);
-      const int64_t bi = row * a.w.ld_absmax + blk;
-      if (NESTED) {
-        st.sraw[rt][h] = __ldg(static_cast<const uint8_t*>(a.w.absmax) + bi);
-        const int64_t gb = a.w.gblk_base + row * a.w.gblk_row_stride + blk;
-        st.a2[rt][h] = __ldg(a.w.absmax2 + (gb >> 8));
-      } else {
-        st.sraw[rt][h] = __float_as_uint(__ldg(static_cast<const float*>(a.w.absmax) + bi));
-      }
-    }
-  }
+      const int64_t row = static_cast<int64_t>(grp) * (16 * RT) + rt * 16 + h * 8 + g;
+      const uint8_t* p = a.w.packed + row * a.w.ld_packed + unit * (CB * 32) + tq * 8;
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int tok = nt * 8 + g;
-    if (tok < a.M) {
-      const T* p = x + tok * a.ldx + blk * 64 + tq * 16;
-      st.xv[nt][0] = ldg_u4(p);
-      st.xv[nt][1] = ldg_u4(p + 8);
-    } else {
-      st.xv[nt][0] = make_uint4(0, 0, 0, 0);
-      st.xv[nt][1] = make_uint4(0, 0, 0, 0);
+      for (int j = 0; j < CB; ++j) b.w[rt][h][j] = ldg_stream_u2(p + 32 * j);
     }
   }
 }
 
-template <typename T, int RT, int NT, bool NESTED>
-__device__ __forceinline__ void compute_stage(const Stage<RT, NT>& st, float (&acc)[RT][NT][4],
-                                              const uint32_t* lutp, const float* code2_s, float offset) {
+__device__ __forceinline__ uint32_t lut_lookup(const uint8_t* lut, uint32_t word, uint32_t lane4, uint32_t sel) {
+  return *reinterpret_cast<const uint32_t*>(lut + __byte_perm(word, lane4, sel));
+}
+
+// Scales of the CB blocks of rows (g, g+8) of each tile, for unit `unit` of group `grp`.
+template <int RT, int CB, bool NESTED>
+__device__ __forceinline__ void load_scales(float (&sc)[RT][2][CB], const GemmArgs& a, int grp, int unit,
+                                            const float* code2_s, int g) {
 #pragma unroll
   for (int rt = 0; rt < RT; ++rt) {
-    float c[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const uint32_t wg = (s < 2) ? st.w[rt][0].x : st.w[rt][0].y;
-      const uint32_t wh = (s < 2) ? st.w[rt][1].x : st.w[rt][1].y;
-      const int sh = (s & 1) * 2;
-      const uint32_t a0 = lutp[byte_of(wg, sh) << 5];
-      const uint32_t a2 = lutp[byte_of(wg, sh + 1) << 5];
-      const uint32_t a1 = lutp[byte_of(wh, sh) << 5];
-      const uint32_t a3 = lutp[byte_of(wh, sh + 1) << 5];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint32_t* xw = reinterpret_cast<const uint32_t*>(&st.xv[nt][0]);
-        Mma<T>::run(c[nt], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
-      }
-    }
-    float sc[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      const int64_t row = static_cast<int64_t>(grp) * (16 * RT) + rt * 16 + h * 8 + g;
+      const int64_t bi = row * a.w.ld_absmax + static_cast<int64_t>(unit) * CB;
       if (NESTED) {
-        sc[h] = __fadd_rn(__fmul_rn(code2_s[st.sraw[rt][h]], st.a2[rt][h]), offset);
+        const uint8_t* q = static_cast<const uint8_t*>(a.w.absmax) + bi;
+        // a chunk never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
+        const float a2 = __ldg(a.w.absmax2 + ((a.w.gblk_base + row * a.w.gblk_row_stride + unit * CB) >> 8));
+        if (CB == 4) {
+          const uint32_t q4 = __ldg(reinterpret_cast<const uint32_t*>(q));
+#pragma unroll
+          for (int j = 0; j < CB; ++j)
+            sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[(q4 >> (8 * j)) & 0xFF], a2), a.w.offset);
+        } else {
+#pragma unroll
+          for (int j = 0; j < CB; ++j) sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[__ldg(q + j)], a2), a.w.offset);
+        }
       } else {
-        sc[h] = __uint_as_float(st.sraw[rt][h]);
+        const float* s = static_cast<const float*>(a.w.absmax) + bi;
+        if (CB == 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(s));
+          sc[rt][h][0] = v.x; sc[rt][h][CB > 1 ? 1 : 0] = v.y;
+          sc[rt][h][CB > 2 ? 2 : 0] = v.z; sc[rt][h][CB > 3 ? 3 : 0] = v.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < CB; ++j) sc[rt][h][j] = __ldg(s + j);
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int RT, int NT, int CB, bool NESTED>
+__device__ __forceinline__ void compute_unit(const WBuf<RT, CB>& b, const GemmArgs& a, int grp, int unit,
+                                             float (&acc)[RT][NT][4], const uint8_t* lut, uint32_t lane4,
+                                             const float* code2_s, int g, int tq) {
+  float sc[RT][2][CB];
+  load_scales<RT, CB, NESTED>(sc, a, grp, unit, code2_s, g);
+  const T* x = static_cast<const T*>(a.x);
+#pragma unroll
+  for (int j = 0; j < CB; ++j) {
+    const int blk = unit * CB + j;
+    uint4 xv[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tok = nt * 8 + g;
+      if (tok < a.M) {
+        const T* p = x + tok * a.ldx + blk * 64 + tq * 16;
+        xv[nt][0] = ldg_u4(p);
+        xv[nt][1] = ldg_u4(p + 8);
+      } else {
+        xv[nt][0] = make_uint4(0, 0, 0, 0);
+        xv[nt][1] = make_uint4(0, 0, 0, 0);
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      acc[rt][nt][0] = fmaf(sc[0], c[nt][0], acc[rt][nt][0]);
-      acc[rt][nt][1] = fmaf(sc[0], c[nt][1], acc[rt][nt][1]);
-      acc[rt][nt][2] = fmaf(sc[1], c[nt][2], acc[rt][nt][2]);
-      acc[rt][nt][3] = fmaf(sc[1], c[nt][3], acc[rt][nt][3]);
+    for (int rt = 0; rt < RT; ++rt) {
+      float c[NT][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const uint32_t wg = (s < 2) ? b.w[rt][0][j].x : b.w[rt][0][j].y;
+        const uint32_t wh = (s < 2) ? b.w[rt][1][j].x : b.w[rt][1][j].y;
+        const uint32_t sel0 = (s & 1) ? 0x5524u : 0x5504u;   // byte 2(s&1) into bits 8..15, 4*lane below
+        const uint32_t sel1 = (s & 1) ? 0x5534u : 0x5514u;   // byte 2(s&1)+1
+        const uint32_t a0 = lut_lookup(lut, wg, lane4, sel0);
+        const uint32_t a2 = lut_lookup(lut, wg, lane4, sel1);
+        const uint32_t a1 = lut_lookup(lut, wh, lane4, sel0);
+        const uint32_t a3 = lut_lookup(lut, wh, lane4, sel1);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[nt][0]);
+          if (s == 0) Mma<T>::run0(c[nt], a0, a1, a2, a3, xw[0], xw[1]);
+          else Mma<T>::run(c[nt], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[rt][nt][0] = fmaf(sc[rt][0][j], c[nt][0], acc[rt][nt][0]);
+        acc[rt][nt][1] = fmaf(sc[rt][0][j], c[nt][1], acc[rt][nt][1]);
+        acc[rt][nt][2] = fmaf(sc[rt][1][j], c[nt][2], acc[rt][nt][2]);
+        acc[rt][nt][3] = fmaf(sc[rt][1][j], c[nt][3], acc[rt][nt][3]);
+      }
     }
   }
 }
@@ -147,12 +180,12 @@ __device__ __forceinline__ void compute_stage(const Stage<RT, NT>& st, float (&a
 // Store a finished 16*RT-row group held in fragment order (thread g,t owns rows g, g+8 of each
 // tile and tokens 2t, 2t+1 of each n8 tile).
 template <typename OT, int RT, int NT>
-__device__ __forceinline__ void store_group(const GemmArgs& a, int64_t grp, const float (&v)[RT][NT][4],
+__device__ __forceinline__ void store_group(const GemmArgs& a, int grp, const float (&v)[RT][NT][4],
                                             int g, int tq) {
   OT* y = static_cast<OT*>(a.y);
 #pragma unroll
   for (int rt = 0; rt < RT; ++rt) {
-    const int64_t r0 = grp * (16 * RT) + rt * 16 + g;
+    const int64_t r0 = static_cast<int64_t>(grp) * (16 * RT) + rt * 16 + g;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int t0 = nt * 8 + 2 * tq;
@@ -168,61 +201,71 @@ __device__ __forceinline__ void store_group(const GemmArgs& a, int64_t grp, cons
   }
 }
 
-__device__ __forceinline__ int64_t cta_begin(int64_t c, int64_t total, int64_t grid) { return c * total / grid; }
-// CTA whose slice contains pair p: the largest c with floor(c*total/grid) <= p.
-__device__ __forceinline__ int64_t cta_of(int64_t p, int64_t total, int64_t grid) {
-  return ((p + 1) * grid - 1) / total;
+template <int RT, int NT>
+__device__ __forceinline__ void zero_acc(float (&acc)[RT][NT][4]) {
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[rt][nt][0] = acc[rt][nt][1] = acc[rt][nt][2] = acc[rt][nt][3] = 0.f;
 }
 
-template <typename T, typename OT, int RT, int NT, bool NESTED, int P>
-__global__ void __launch_bounds__(kGemmThreads, 1) nf4_gemm_tc_kernel(const GemmArgs a) {
+// Unit ranges use 32-bit arithmetic (the host guarantees total * grid < 2^31): the serial parts of
+// the kernel must not pay for 64-bit division.
+__device__ __forceinline__ int cta_begin(int c, int total, int grid) { return c * total / grid; }
+// CTA whose slice contains unit p: the largest c with floor(c*total/grid) <= p.
+__device__ __forceinline__ int cta_of(int p, int total, int grid) { return ((p + 1) * grid - 1) / total; }
+
+template <typename T, typename OT, int RT, int NT, int CB, bool NESTED, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs a) {
   constexpr int E = RT * NT * 128;  // fp32 values of one group partial, in fragment order
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
-  float* code2_s = reinterpret_cast<float*>(smem + kLutWords * 4);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint8_t* lut = smem;
+  float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);
   float* slots = code2_s + 256;  // [warps][2][E]
+  __shared__ int s_wa[NW], s_wb[NW], s_fg[NW], s_lg[NW];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
 
-  for (int i = tid; i < kLutWords; i += kGemmThreads) {
-    const int e = i >> 5;
-    lut[i] = Dt<T>::pack2(__ldg(a.w.code + (e >> 4)), __ldg(a.w.code + (e & 15)));
+  const int grid = gridDim.x, cta = blockIdx.x;
+  const int A = cta_begin(cta, a.total, grid), B = cta_begin(cta + 1, a.total, grid);
+  const int wa = A + warp * (B - A) / NW;
+  const int wb = A + (warp + 1) * (B - A) / NW;
+  const int upg = a.upg;
+  const int first_grp = wa / upg;
+  if (lane == 0) {
+    s_wa[warp] = wa;
+    s_wb[warp] = wb;
+    s_fg[warp] = first_grp;
+    s_lg[warp] = wb > wa ? (wb - 1) / upg : -1;
+  }
+
+  // first unit's weights in flight while the table is built
+  WBuf<RT, CB> buf0, buf1;
+  int lgrp = first_grp;
+  int lun = wa - lgrp * upg;
+  if (wa < wb) load_w<RT, CB>(buf0, a, lgrp, lun, g, tq);
+  if (++lun == upg) { lun = 0; ++lgrp; }
+
+  for (int i = tid; i < 256 * 32; i += NW * 32) {
+    const int e = i >> 5, l = i & 31;
+    *reinterpret_cast<uint32_t*>(smem + e * kLutEntryBytes + l * 4) =
+        Dt<T>::pack2(__ldg(a.w.code + (e >> 4)), __ldg(a.w.code + (e & 15)));
   }
   if (NESTED) {
-    for (int i = tid; i < 256; i += kGemmThreads) code2_s[i] = __ldg(a.w.code2 + i);
+    for (int i = tid; i < 256; i += NW * 32) code2_s[i] = __ldg(a.w.code2 + i);
   }
   __syncthreads();
 
-  const int64_t grid = gridDim.x, cta = blockIdx.x;
-  const int64_t A = cta_begin(cta, a.total, grid), B = cta_begin(cta + 1, a.total, grid);
-  const int64_t wa = A + warp * (B - A) / kGemmWarps;
-  const int64_t wb = A + (warp + 1) * (B - A) / kGemmWarps;
-  const int kb = a.kb;
-  const uint32_t* lutp = lut + lane;
-
   if (wa < wb) {
-    Stage<RT, NT> st[P];
-    // load cursor
-    int64_t lgrp = wa / kb;
-    int lblk = static_cast<int>(wa - lgrp * kb);
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      if (wa + j < wb) load_stage<T, RT, NT, NESTED>(st[j], a, lgrp, lblk, g, tq);
-      if (++lblk == kb) { lblk = 0; ++lgrp; }
-    }
     float acc[RT][NT][4];
-#pragma unroll
-    for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[rt][nt][0] = acc[rt][nt][1] = acc[rt][nt][2] = acc[rt][nt][3] = 0.f;
+    zero_acc(acc);
+    int cgrp = first_grp;
+    int cun = wa - cgrp * upg;
 
-    const int64_t first_grp = wa / kb;
-    int64_t cgrp = first_grp;
-    int cblk = static_cast<int>(wa - cgrp * kb);
-
-    auto flush = [&](int64_t grp) {
-      const bool full = grp * kb >= wa && (grp + 1) * kb <= wb;
+    auto flush = [&](int grp) {
+      const bool full = grp * upg >= wa && (grp + 1) * upg <= wb;
       if (full) {
         store_group<OT, RT, NT>(a, grp, acc, g, tq);
       } else {
@@ -234,46 +277,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nf4_gemm_tc_kernel(const Gemm
             *reinterpret_cast<float4*>(s + (rt * NT + nt) * 128) =
                 make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]);
       }
-#pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[rt][nt][0] = acc[rt][nt][1] = acc[rt][nt][2] = acc[rt][nt][3] = 0.f;
+      zero_acc(acc);
     };
-
-    for (int64_t base = wa; base < wb; base += P) {
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        if (base + j < wb) {
-          compute_stage<T, RT, NT, NESTED>(st[j], acc, lutp, code2_s, a.w.offset);
-          if (base + j + P < wb) load_stage<T, RT, NT, NESTED>(st[j], a, lgrp, lblk, g, tq);
-          if (++lblk == kb) { lblk = 0; ++lgrp; }
-          if (++cblk == kb) {
-            flush(cgrp);
-            cblk = 0;
-            ++cgrp;
-          }
-        }
+    auto step = [&](WBuf<RT, CB>& cur, WBuf<RT, CB>& nxt, int p) {
+      if (p + 1 < wb) {
+        load_w<RT, CB>(nxt, a, lgrp, lun, g, tq);
+        if (++lun == upg) { lun = 0; ++lgrp; }
       }
+      compute_unit<T, RT, NT, CB, NESTED>(cur, a, cgrp, cun, acc, lut, lane4, code2_s, g, tq);
+      if (++cun == upg) {
+        flush(cgrp);
+        cun = 0;
+        ++cgrp;
+      }
+    };
+    for (int p = wa; p < wb; p += 2) {
+      step(buf0, buf1, p);
+      if (p + 1 < wb) step(buf1, buf0, p + 1);
     }
-    if (cblk != 0) flush(cgrp);  // range ended inside a group
+    if (cun != 0) flush(cgrp);  // range ended inside a group
   }
   __syncthreads();
 
   // ---- combine the warp partials of this CTA (warp 0; lanes own their fragment positions)
   if (warp != 0 || A >= B) return;
-  const int64_t gA = A / kb, gB = (B - 1) / kb;
-  for (int64_t grp = gA; grp <= gB; ++grp) {
+  const int gA = A / upg, gB = (B - 1) / upg;
+  for (int grp = gA; grp <= gB; ++grp) {
     float v[RT][NT][4];
-#pragma unroll
-    for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) v[rt][nt][0] = v[rt][nt][1] = v[rt][nt][2] = v[rt][nt][3] = 0.f;
+    zero_acc(v);
     bool done = false;
-    for (int w = 0; w < kGemmWarps; ++w) {
-      const int64_t xa = A + w * (B - A) / kGemmWarps, xb = A + (w + 1) * (B - A) / kGemmWarps;
+    for (int w = 0; w < NW; ++w) {
+      const int xa = s_wa[w], xb = s_wb[w];
       if (xa >= xb) continue;
-      if (grp * kb >= xa && (grp + 1) * kb <= xb) { done = true; break; }
-      const int64_t fg = xa / kb, lg = (xb - 1) / kb;
+      if (grp * upg >= xa && (grp + 1) * upg <= xb) { done = true; break; }
+      const int fg = s_fg[w], lg = s_lg[w];
       if (grp < fg || grp > lg) continue;
       const float* s = slots + (w * 2 + (grp == fg ? 0 : 1)) * E + lane * 4;
 #pragma unroll
@@ -285,39 +322,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nf4_gemm_tc_kernel(const Gemm
         }
     }
     if (done) continue;
-    if (grp * kb >= A && (grp + 1) * kb <= B) {
+    if (grp * upg >= A && (grp + 1) * upg <= B) {
       store_group<OT, RT, NT>(a, grp, v, g, tq);
       continue;
     }
-    // group shared with neighbouring CTAs: publish this CTA's partial, last arriver reduces
-    float* mine = a.partials + (cta * 2 + (grp == gA ? 0 : 1)) * E + lane * 4;
+    // group shared with neighbouring CTAs: publish this CTA's partial; the last arriver reduces.
+    // The lanes' stores are ordered before lane 0's release by the warp barrier; lane 0's acquire
+    // (and the barrier after it) orders the last arriver's reads after every published partial.
+    float* mine = a.partials + (static_cast<int64_t>(cta) * 2 + (grp == gA ? 0 : 1)) * E + lane * 4;
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
         __stcg(reinterpret_cast<float4*>(mine + (rt * NT + nt) * 128),
                make_float4(v[rt][nt][0], v[rt][nt][1], v[rt][nt][2], v[rt][nt][3]));
-    __threadfence();
     __syncwarp();
-    const int64_t c_lo = cta_of(grp * kb, a.total, grid), c_hi = cta_of((grp + 1) * kb - 1, a.total, grid);
+    const int c_lo = cta_of(grp * upg, a.total, grid), c_hi = cta_of((grp + 1) * upg - 1, a.total, grid);
     int last = 0;
     if (lane == 0) {
-      const int old = atomicAdd(a.counters + grp, 1);
-      if (old == static_cast<int>(c_hi - c_lo)) {
+      const int old = atomic_add_acq_rel_gpu(a.counters + grp, 1);
+      if (old == c_hi - c_lo) {
         last = 1;
-        a.counters[grp] = 0;
+        a.counters[grp] = 0;   // every contributor has arrived: reset for the next launch
       }
     }
     last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
     if (!last) continue;
-    __threadfence();
-#pragma unroll
-    for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) v[rt][nt][0] = v[rt][nt][1] = v[rt][nt][2] = v[rt][nt][3] = 0.f;
-    for (int64_t c = c_lo; c <= c_hi; ++c) {
-      const int64_t cfirst = cta_begin(c, a.total, grid) / kb;
-      const float* s = a.partials + (c * 2 + (grp == cfirst ? 0 : 1)) * E + lane * 4;
+    zero_acc(v);
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const int cfirst = cta_begin(c, a.total, grid) / upg;
+      const float* s = a.partials + (static_cast<int64_t>(c) * 2 + (grp == cfirst ? 0 : 1)) * E + lane * 4;
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -409,52 +444,70 @@ constexpr size_t kCounterBytes = 64 * 1024;
 constexpr int64_t kMaxGroups = kCounterBytes / 4;
 
 struct GemmConfig {
-  int rt, nt;
+  int rt, nt, cb, nw;
   int64_t groups, total;
   int grid;
   size_t counter_bytes, partial_bytes;
 };
 
-int choose_config(int M, int N, int K, const DeviceInfo& di, GemmConfig* c) {
+bool chunk4_ok(int K, const void* absmax, int64_t ld_absmax, int nested, int64_t gblk_base, int64_t gblk_row_stride) {
+  if ((K / 64) % 4 != 0 || ld_absmax % 4 != 0) return false;
+  if (nested) return aligned(absmax, 4) && gblk_base % 4 == 0 && gblk_row_stride % 4 == 0;
+  return aligned(absmax, 16);
+}
+
+int choose_config(int M, int N, int K, bool chunk4, const DeviceInfo& di, GemmConfig* c) {
   c->nt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
   c->rt = (c->nt == 1 && N % 32 == 0) ? 2 : 1;
+  c->cb = chunk4 ? 4 : 1;
+  c->nw = c->nt > 2 ? 8 : (c->rt == 2 ? 12 : 16);
   c->groups = N / (16 * c->rt);
-  c->total = c->groups * (K / 64);
+  c->total = c->groups * (K / (64 * c->cb));
   int64_t grid = di.sm_count;
   if (grid > c->total) grid = c->total;
   if (grid < 1) grid = 1;
   c->grid = static_cast<int>(grid);
   c->counter_bytes = kCounterBytes;
   c->partial_bytes = static_cast<size_t>(c->grid) * 2 * (c->rt * c->nt * 128) * 4;
-  return c->groups <= kMaxGroups ? B2D_OK : B2D_ERR_SHAPE;
+  if (c->groups > kMaxGroups || c->total * static_cast<int64_t>(c->grid) >= (int64_t(1) << 31)) return B2D_ERR_SHAPE;
+  return B2D_OK;
 }
 
-size_t gemm_smem_bytes(int rt, int nt) {
-  return kLutWords * 4 + 256 * 4 + static_cast<size_t>(kGemmWarps) * 2 * rt * nt * 128 * 4;
+size_t gemm_smem_bytes(int rt, int nt, int nw) {
+  return kLutBytes + kCode2Bytes + static_cast<size_t>(nw) * 2 * rt * nt * 128 * 4;
 }
 
-template <typename T, typename OT, int RT, int NT, bool NESTED, int P>
+template <typename T, typename OT, int RT, int NT, int CB, bool NESTED, int NW>
 int launch_tc(const GemmArgs& a, int grid, cudaStream_t stream) {
-  auto kern = nf4_gemm_tc_kernel<T, OT, RT, NT, NESTED, P>;
-  const size_t smem = gemm_smem_bytes(RT, NT);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
-  kern<<<grid, kGemmThreads, smem, stream>>>(a);
+  auto kern = nf4_gemm_tc_kernel<T, OT, RT, NT, CB, NESTED, NW>;
+  const size_t smem = gemm_smem_bytes(RT, NT, NW);
+  static bool configured[64] = {false};   // per device; setting it twice is harmless
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B2D_ERR_DEVICE;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
+    configured[dev] = true;
+  }
+  kern<<<grid, NW * 32, smem, stream>>>(a);
   return launch_status();
 }
 
-template <typename T, typename OT, bool NESTED>
-int dispatch_tc(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
+template <typename T, typename OT, int CB, bool NESTED>
+int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
   if (c.nt == 1)
-    return c.rt == 2 ? launch_tc<T, OT, 2, 1, NESTED, 4>(a, c.grid, s) : launch_tc<T, OT, 1, 1, NESTED, 6>(a, c.grid, s);
-  if (c.nt == 2) return launch_tc<T, OT, 1, 2, NESTED, 4>(a, c.grid, s);
-  if (c.nt == 4) return launch_tc<T, OT, 1, 4, NESTED, 2>(a, c.grid, s);
-  return launch_tc<T, OT, 1, 8, NESTED, 2>(a, c.grid, s);
+    return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 12>(a, c.grid, s)
+                     : launch_tc<T, OT, 1, 1, CB, NESTED, 16>(a, c.grid, s);
+  if (c.nt == 2) return launch_tc<T, OT, 1, 2, CB, NESTED, 16>(a, c.grid, s);
+  if (c.nt == 4) return launch_tc<T, OT, 1, 4, CB, NESTED, 8>(a, c.grid, s);
+  return launch_tc<T, OT, 1, 8, CB, NESTED, 8>(a, c.grid, s);
 }
 
 template <typename T, typename OT>
-int dispatch_tc_n(const GemmArgs& a, const GemmConfig& c, int nested, cudaStream_t s) {
-  return nested ? dispatch_tc<T, OT, true>(a, c, s) : dispatch_tc<T, OT, false>(a, c, s);
+int dispatch_tc(const GemmArgs& a, const GemmConfig& c, int nested, cudaStream_t s) {
+  if (c.cb == 4)
+    return nested ? dispatch_tc_cb<T, OT, 4, true>(a, c, s) : dispatch_tc_cb<T, OT, 4, false>(a, c, s);
+  return nested ? dispatch_tc_cb<T, OT, 1, true>(a, c, s) : dispatch_tc_cb<T, OT, 1, false>(a, c, s);
 }
 
 int check_weight_args(const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed, const void* absmax,
@@ -484,7 +537,8 @@ extern "C" size_t b2d_nf4_gemm_workspace_bytes(int M, int N, int K) {
   if (device_info(&di) != B2D_OK) return 0;
   if (M <= 0 || N <= 0 || K <= 0 || N % 16 || K % 64) return 0;
   GemmConfig c;
-  if (choose_config(M, N, K, di, &c) != B2D_OK) return 0;
+  // the 1-block chunking has the most units, hence the largest grid: size for it
+  if (choose_config(M, N, K, false, di, &c) != B2D_OK) return 0;
   return c.counter_bytes + c.partial_bytes;
 }
 
@@ -499,7 +553,8 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   DeviceInfo di;
   if ((st = device_info(&di)) != B2D_OK) return st;
   GemmConfig c;
-  if ((st = choose_config(M, N, K, di, &c)) != B2D_OK) return st;
+  const bool c4 = chunk4_ok(K, absmax, ld_absmax, nested, gblk_base, gblk_row_stride);
+  if ((st = choose_config(M, N, K, c4, di, &c)) != B2D_OK) return st;
   if (!workspace || workspace_bytes < c.counter_bytes + c.partial_bytes) return B2D_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return B2D_ERR_ALIGN;
   GemmArgs a;
@@ -507,16 +562,16 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   a.w = Nf4View{packed, ld_packed, absmax, ld_absmax, code2, absmax2, offset, gblk_base, gblk_row_stride, code};
   a.y = y; a.ldy = ldy;
   a.M = M; a.N = N; a.K = K;
-  a.kb = K / 64;
-  a.groups = c.groups;
-  a.total = c.total;
+  a.upg = K / (64 * c.cb);
+  a.groups = static_cast<int>(c.groups);
+  a.total = static_cast<int>(c.total);
   a.counters = static_cast<int*>(workspace);
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + c.counter_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == B2D_F16)
-    return y_dtype == B2D_F32 ? dispatch_tc_n<__half, float>(a, c, nested, s) : dispatch_tc_n<__half, __half>(a, c, nested, s);
-  return y_dtype == B2D_F32 ? dispatch_tc_n<__nv_bfloat16, float>(a, c, nested, s)
-                            : dispatch_tc_n<__nv_bfloat16, __nv_bfloat16>(a, c, nested, s);
+    return y_dtype == B2D_F32 ? dispatch_tc<__half, float>(a, c, nested, s) : dispatch_tc<__half, __half>(a, c, nested, s);
+  return y_dtype == B2D_F32 ? dispatch_tc<__nv_bfloat16, float>(a, c, nested, s)
+                            : dispatch_tc<__nv_bfloat16, __nv_bfloat16>(a, c, nested, s);
 }
 
 namespace b2d {
