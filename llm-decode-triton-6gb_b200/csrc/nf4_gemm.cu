@@ -241,21 +241,30 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
     s_lg[warp] = wb > wa ? (wb - 1) / upg : -1;
   }
 
-  // first unit's weights in flight while the table is built
+  // table inputs first, then the first unit's weights, all in flight while the table is built
+  const float my_code = __ldg(a.w.code + (lane & 15));
+  float my_code2 = 0.f;
+  if (NESTED && tid < 256) my_code2 = __ldg(a.w.code2 + tid);
   WBuf<RT, CB> buf0, buf1;
   int lgrp = first_grp;
   int lun = wa - lgrp * upg;
   if (wa < wb) load_w<RT, CB>(buf0, a, lgrp, lun, g, tq);
   if (++lun == upg) { lun = 0; ++lgrp; }
 
-  for (int i = tid; i < 256 * 32; i += NW * 32) {
-    const int e = i >> 5, l = i & 31;
-    *reinterpret_cast<uint32_t*>(smem + e * kLutEntryBytes + l * 4) =
-        Dt<T>::pack2(__ldg(a.w.code + (e >> 4)), __ldg(a.w.code + (e & 15)));
+  // Warps 0..7 build the table: lane l of warp w computes entry e = 32w + l once and writes its 32
+  // lane copies in a lane-rotated order, so every store instruction hits 32 distinct banks.
+  {
+    const int e = warp * 32 + lane;
+    const float hi = __shfl_sync(0xffffffffu, my_code, (e >> 4) & 15);
+    const float lo = __shfl_sync(0xffffffffu, my_code, e & 15);
+    if (warp < 8) {
+      const uint32_t val = Dt<T>::pack2(hi, lo);
+      uint32_t* entry = reinterpret_cast<uint32_t*>(smem + e * kLutEntryBytes);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) entry[(i + lane) & 31] = val;
+    }
   }
-  if (NESTED) {
-    for (int i = tid; i < 256; i += NW * 32) code2_s[i] = __ldg(a.w.code2 + i);
-  }
+  if (NESTED && tid < 256) code2_s[tid] = my_code2;
   __syncthreads();
 
   if (wa < wb) {
@@ -299,20 +308,21 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
   }
   __syncthreads();
 
-  // ---- combine the warp partials of this CTA (warp 0; lanes own their fragment positions)
-  if (warp != 0 || A >= B) return;
+  // ---- combine: warp i handles the i-th row group this CTA touched (lanes own their fragment
+  // positions). Its contributing warps are the contiguous range holding the group's units.
+  if (A >= B) return;
   const int gA = A / upg, gB = (B - 1) / upg;
-  for (int grp = gA; grp <= gB; ++grp) {
+  const int span = B - A;
+  for (int grp = gA + warp; grp <= gB; grp += NW) {
+    const int lo = max(grp * upg, A), hi = min((grp + 1) * upg, B);   // this CTA's units of grp
+    const bool shared = grp * upg < A || (grp + 1) * upg > B;          // other CTAs hold the rest
+    const int w_lo = ((lo - A + 1) * NW - 1) / span, w_hi = ((hi - 1 - A + 1) * NW - 1) / span;
+    if (!shared && w_lo == w_hi) continue;                            // one warp stored it in full
     float v[RT][NT][4];
     zero_acc(v);
-    bool done = false;
-    for (int w = 0; w < NW; ++w) {
-      const int xa = s_wa[w], xb = s_wb[w];
-      if (xa >= xb) continue;
-      if (grp * upg >= xa && (grp + 1) * upg <= xb) { done = true; break; }
-      const int fg = s_fg[w], lg = s_lg[w];
-      if (grp < fg || grp > lg) continue;
-      const float* s = slots + (w * 2 + (grp == fg ? 0 : 1)) * E + lane * 4;
+    for (int w = w_lo; w <= w_hi; ++w) {
+      if (s_wa[w] >= s_wb[w]) continue;   // a warp without units (CTA slice shorter than NW)
+      const float* s = slots + (w * 2 + (grp == s_fg[w] ? 0 : 1)) * E + lane * 4;
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -321,14 +331,13 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
           v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
         }
     }
-    if (done) continue;
-    if (grp * upg >= A && (grp + 1) * upg <= B) {
+    if (!shared) {
       store_group<OT, RT, NT>(a, grp, v, g, tq);
       continue;
     }
-    // group shared with neighbouring CTAs: publish this CTA's partial; the last arriver reduces.
-    // The lanes' stores are ordered before lane 0's release by the warp barrier; lane 0's acquire
-    // (and the barrier after it) orders the last arriver's reads after every published partial.
+    // Shared with neighbouring CTAs: publish this CTA's partial; the last arriver adds all partials
+    // in CTA order. The lanes' stores are ordered before lane 0's release by the warp barrier; lane
+    // 0's acquire (and the barrier after it) orders the last arriver's reads after every partial.
     float* mine = a.partials + (static_cast<int64_t>(cta) * 2 + (grp == gA ? 0 : 1)) * E + lane * 4;
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt)
@@ -339,12 +348,9 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
     __syncwarp();
     const int c_lo = cta_of(grp * upg, a.total, grid), c_hi = cta_of((grp + 1) * upg - 1, a.total, grid);
     int last = 0;
-    if (lane == 0) {
-      const int old = atomic_add_acq_rel_gpu(a.counters + grp, 1);
-      if (old == c_hi - c_lo) {
-        last = 1;
-        a.counters[grp] = 0;   // every contributor has arrived: reset for the next launch
-      }
+    if (lane == 0 && atomic_add_acq_rel_gpu(a.counters + grp, 1) == c_hi - c_lo) {
+      last = 1;
+      a.counters[grp] = 0;   // every contributor has arrived: reset for the next launch
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     __syncwarp();
