@@ -62,13 +62,36 @@ struct GemmArgs {
   int* counters;     // [groups]
 };
 
-template <int RT, int CB>
+// One unit of work for one thread, loaded a unit ahead: its weight bytes, the raw per-block scales
+// of its rows and (for M <= 8) the activations of the unit's first block.
+template <int RT, int NT, int CB, bool NESTED>
 struct WBuf {
-  uint2 w[RT][2][CB];    // rows g, g+8 of each 16-row tile; this thread's 8 bytes of each block
+  uint2 w[RT][2][CB];                       // rows g, g+8 of each 16-row tile; 8 bytes per block
+  uint32_t sq[RT][2][NESTED ? 1 : CB];      // double quant: CB uint8 indices packed; else fp32 bits
+  float a2[RT][2];                          // double quant: absmax2 of the row's 256-block group
+  uint4 x0[NT == 1 ? 1 : 1][2];             // activations of block 0 (used when NT == 1)
 };
 
-template <int RT, int CB>
-__device__ __forceinline__ void load_w(WBuf<RT, CB>& b, const GemmArgs& a, int grp, int unit, int g, int tq) {
+template <typename T, int NT>
+__device__ __forceinline__ void load_x(uint4 (&xv)[NT][2], const GemmArgs& a, int blk, int g, int tq) {
+  const T* x = static_cast<const T*>(a.x);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = nt * 8 + g;
+    if (tok < a.M) {
+      const T* p = x + tok * a.ldx + blk * 64 + tq * 16;
+      xv[nt][0] = ldg_u4(p);
+      xv[nt][1] = ldg_u4(p + 8);
+    } else {
+      xv[nt][0] = make_uint4(0, 0, 0, 0);
+      xv[nt][1] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <typename T, int RT, int NT, int CB, bool NESTED>
+__device__ __forceinline__ void load_w(WBuf<RT, NT, CB, NESTED>& b, const GemmArgs& a, int grp, int unit, int g,
+                                       int tq) {
 #pragma unroll
   for (int rt = 0; rt < RT; ++rt) {
 #pragma unroll
@@ -77,7 +100,29 @@ __device__ __forceinline__ void load_w(WBuf<RT, CB>& b, const GemmArgs& a, int g
       const uint8_t* p = a.w.packed + row * a.w.ld_packed + unit * (CB * 32) + tq * 8;
 #pragma unroll
       for (int j = 0; j < CB; ++j) b.w[rt][h][j] = ldg_stream_u2(p + 32 * j);
+      const int64_t bi = row * a.w.ld_absmax + static_cast<int64_t>(unit) * CB;
+      if (NESTED) {
+        const uint8_t* q = static_cast<const uint8_t*>(a.w.absmax) + bi;
+        b.sq[rt][h][0] = CB == 4 ? __ldg(reinterpret_cast<const uint32_t*>(q)) : static_cast<uint32_t>(__ldg(q));
+        // a chunk never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
+        b.a2[rt][h] = __ldg(a.w.absmax2 + ((a.w.gblk_base + row * a.w.gblk_row_stride + unit * CB) >> 8));
+      } else {
+        const float* sp = static_cast<const float*>(a.w.absmax) + bi;
+        if (CB == 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(sp));
+          b.sq[rt][h][0] = __float_as_uint(v.x);
+          b.sq[rt][h][CB > 1 ? 1 : 0] = __float_as_uint(v.y);
+          b.sq[rt][h][CB > 2 ? 2 : 0] = __float_as_uint(v.z);
+          b.sq[rt][h][CB > 3 ? 3 : 0] = __float_as_uint(v.w);
+        } else {
+          b.sq[rt][h][0] = __float_as_uint(__ldg(sp));
+        }
+      }
     }
+  }
+  if (NT == 1) {
+    uint4 (&x0)[1][2] = reinterpret_cast<uint4 (&)[1][2]>(b.x0);
+    load_x<T, 1>(x0, a, unit * CB, g, tq);
   }
 }
 
@@ -85,69 +130,32 @@ __device__ __forceinline__ uint32_t lut_lookup(const uint8_t* lut, uint32_t word
   return *reinterpret_cast<const uint32_t*>(lut + __byte_perm(word, lane4, sel));
 }
 
-// Scales of the CB blocks of rows (g, g+8) of each tile, for unit `unit` of group `grp`.
-template <int RT, int CB, bool NESTED>
-__device__ __forceinline__ void load_scales(float (&sc)[RT][2][CB], const GemmArgs& a, int grp, int unit,
-                                            const float* code2_s, int g) {
-#pragma unroll
-  for (int rt = 0; rt < RT; ++rt) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int64_t row = static_cast<int64_t>(grp) * (16 * RT) + rt * 16 + h * 8 + g;
-      const int64_t bi = row * a.w.ld_absmax + static_cast<int64_t>(unit) * CB;
-      if (NESTED) {
-        const uint8_t* q = static_cast<const uint8_t*>(a.w.absmax) + bi;
-        // a chunk never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
-        const float a2 = __ldg(a.w.absmax2 + ((a.w.gblk_base + row * a.w.gblk_row_stride + unit * CB) >> 8));
-        if (CB == 4) {
-          const uint32_t q4 = __ldg(reinterpret_cast<const uint32_t*>(q));
-#pragma unroll
-          for (int j = 0; j < CB; ++j)
-            sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[(q4 >> (8 * j)) & 0xFF], a2), a.w.offset);
-        } else {
-#pragma unroll
-          for (int j = 0; j < CB; ++j) sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[__ldg(q + j)], a2), a.w.offset);
-        }
-      } else {
-        const float* s = static_cast<const float*>(a.w.absmax) + bi;
-        if (CB == 4) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(s));
-          sc[rt][h][0] = v.x; sc[rt][h][CB > 1 ? 1 : 0] = v.y;
-          sc[rt][h][CB > 2 ? 2 : 0] = v.z; sc[rt][h][CB > 3 ? 3 : 0] = v.w;
-        } else {
-#pragma unroll
-          for (int j = 0; j < CB; ++j) sc[rt][h][j] = __ldg(s + j);
-        }
-      }
-    }
-  }
-}
-
 template <typename T, int RT, int NT, int CB, bool NESTED>
-__device__ __forceinline__ void compute_unit(const WBuf<RT, CB>& b, const GemmArgs& a, int grp, int unit,
+__device__ __forceinline__ void compute_unit(const WBuf<RT, NT, CB, NESTED>& b, const GemmArgs& a, int unit,
                                              float (&acc)[RT][NT][4], const uint8_t* lut, uint32_t lane4,
                                              const float* code2_s, int g, int tq) {
-  float sc[RT][2][CB];
-  load_scales<RT, CB, NESTED>(sc, a, grp, unit, code2_s, g);
-  const T* x = static_cast<const T*>(a.x);
+  uint4 xv[NT][2], xn[NT][2];
+  if (NT == 1) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) xv[0][i] = b.x0[0][i];
+  } else {
+    load_x<T, NT>(xv, a, unit * CB, g, tq);
+  }
 #pragma unroll
   for (int j = 0; j < CB; ++j) {
-    const int blk = unit * CB + j;
-    uint4 xv[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int tok = nt * 8 + g;
-      if (tok < a.M) {
-        const T* p = x + tok * a.ldx + blk * 64 + tq * 16;
-        xv[nt][0] = ldg_u4(p);
-        xv[nt][1] = ldg_u4(p + 8);
-      } else {
-        xv[nt][0] = make_uint4(0, 0, 0, 0);
-        xv[nt][1] = make_uint4(0, 0, 0, 0);
-      }
-    }
+    if (j + 1 < CB) load_x<T, NT>(xn, a, unit * CB + j + 1, g, tq);   // next block's activations
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt) {
+      float sc[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (NESTED) {
+          const uint32_t q = CB == 4 ? (b.sq[rt][h][0] >> (8 * j)) & 0xFF : b.sq[rt][h][0];
+          sc[h] = __fadd_rn(__fmul_rn(code2_s[q], b.a2[rt][h]), a.w.offset);
+        } else {
+          sc[h] = __uint_as_float(b.sq[rt][h][NESTED ? 0 : j]);
+        }
+      }
       float c[NT][4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
@@ -168,11 +176,15 @@ __device__ __forceinline__ void compute_unit(const WBuf<RT, CB>& b, const GemmAr
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        acc[rt][nt][0] = fmaf(sc[rt][0][j], c[nt][0], acc[rt][nt][0]);
-        acc[rt][nt][1] = fmaf(sc[rt][0][j], c[nt][1], acc[rt][nt][1]);
-        acc[rt][nt][2] = fmaf(sc[rt][1][j], c[nt][2], acc[rt][nt][2]);
-        acc[rt][nt][3] = fmaf(sc[rt][1][j], c[nt][3], acc[rt][nt][3]);
+        acc[rt][nt][0] = fmaf(sc[0], c[nt][0], acc[rt][nt][0]);
+        acc[rt][nt][1] = fmaf(sc[0], c[nt][1], acc[rt][nt][1]);
+        acc[rt][nt][2] = fmaf(sc[1], c[nt][2], acc[rt][nt][2]);
+        acc[rt][nt][3] = fmaf(sc[1], c[nt][3], acc[rt][nt][3]);
       }
+    }
+    if (j + 1 < CB) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) { xv[nt][0] = xn[nt][0]; xv[nt][1] = xn[nt][1]; }
     }
   }
 }
@@ -245,10 +257,10 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
   const float my_code = __ldg(a.w.code + (lane & 15));
   float my_code2 = 0.f;
   if (NESTED && tid < 256) my_code2 = __ldg(a.w.code2 + tid);
-  WBuf<RT, CB> buf0, buf1;
+  WBuf<RT, NT, CB, NESTED> buf0, buf1;
   int lgrp = first_grp;
   int lun = wa - lgrp * upg;
-  if (wa < wb) load_w<RT, CB>(buf0, a, lgrp, lun, g, tq);
+  if (wa < wb) load_w<T, RT, NT, CB, NESTED>(buf0, a, lgrp, lun, g, tq);
   if (++lun == upg) { lun = 0; ++lgrp; }
 
   // Warps 0..7 build the table: lane l of warp w computes entry e = 32w + l once and writes its 32
@@ -288,12 +300,12 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
       }
       zero_acc(acc);
     };
-    auto step = [&](WBuf<RT, CB>& cur, WBuf<RT, CB>& nxt, int p) {
+    auto step = [&](WBuf<RT, NT, CB, NESTED>& cur, WBuf<RT, NT, CB, NESTED>& nxt, int p) {
       if (p + 1 < wb) {
-        load_w<RT, CB>(nxt, a, lgrp, lun, g, tq);
+        load_w<T, RT, NT, CB, NESTED>(nxt, a, lgrp, lun, g, tq);
         if (++lun == upg) { lun = 0; ++lgrp; }
       }
-      compute_unit<T, RT, NT, CB, NESTED>(cur, a, cgrp, cun, acc, lut, lane4, code2_s, g, tq);
+      compute_unit<T, RT, NT, CB, NESTED>(cur, a, cun, acc, lut, lane4, code2_s, g, tq);
       if (++cun == upg) {
         flush(cgrp);
         cun = 0;
@@ -466,7 +478,7 @@ int choose_config(int M, int N, int K, bool chunk4, const DeviceInfo& di, GemmCo
   c->nt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
   c->rt = (c->nt == 1 && N % 32 == 0) ? 2 : 1;
   c->cb = chunk4 ? 4 : 1;
-  c->nw = c->nt > 2 ? 8 : (c->rt == 2 ? 12 : 16);
+  c->nw = c->nt > 2 ? 8 : (c->nt == 2 ? 12 : (c->rt == 2 ? 10 : 16));
   c->groups = N / (16 * c->rt);
   c->total = c->groups * (K / (64 * c->cb));
   int64_t grid = di.sm_count;
@@ -502,9 +514,9 @@ int launch_tc(const GemmArgs& a, int grid, cudaStream_t stream) {
 template <typename T, typename OT, int CB, bool NESTED>
 int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
   if (c.nt == 1)
-    return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 12>(a, c.grid, s)
+    return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 10>(a, c.grid, s)
                      : launch_tc<T, OT, 1, 1, CB, NESTED, 16>(a, c.grid, s);
-  if (c.nt == 2) return launch_tc<T, OT, 1, 2, CB, NESTED, 16>(a, c.grid, s);
+  if (c.nt == 2) return launch_tc<T, OT, 1, 2, CB, NESTED, 12>(a, c.grid, s);
   if (c.nt == 4) return launch_tc<T, OT, 1, 4, CB, NESTED, 8>(a, c.grid, s);
   return launch_tc<T, OT, 1, 8, CB, NESTED, 8>(a, c.grid, s);
 }
