@@ -1,0 +1,207 @@
+"""Greedy decode of a Mistral-shaped Hugging Face model with NF4 linears on the B200 kernels.
+
+The reference decodes through ``model(input_ids, past_key_values, use_cache=True)`` one token at a
+time (``profiling/common.py:80-85``, ``profiling/04_compare.py:21-31``); HF's ``DynamicCache`` grows
+the KV tensors with ``torch.cat`` every step and Python launches every kernel, so the step cannot be
+replayed as a CUDA graph. This engine keeps the HF modules for the small glue ops (embedding,
+RMSNorm, rotary embedding, SiLU, lm_head, argmax -- the same torch code as the stock path) and
+swaps the two hot paths for the B200 kernels:
+
+* every NF4 linear (q/k/v/o/gate/up/down) -> ``NF4Weight.matmul`` (fused dequant + matmul);
+* attention -> ``decode_attention`` over a static KV cache ``[layers, B, KVH, S_max, D]`` with
+  per-sequence lengths,
+
+and captures one whole decode step (32 layers) in a CUDA graph. Prompts are prefilled through the
+HF forward (the reference's prefill path: SDPA, and dequant + library GEMM for the many-row
+linears); the prompt's K/V are then copied into the static cache.
+"""
+from __future__ import annotations
+
+import torch
+from transformers import MistralConfig, MistralForCausalLM
+from transformers.cache_utils import DynamicCache
+from transformers.models.mistral.modeling_mistral import apply_rotary_pos_emb
+
+from .decode_attention import decode_attention
+from .linear4bit import quantize_model_linears
+from .nf4_gemm import NF4Weight
+
+# Mistral-7B-v0.3 shape (the checkpoint the reference profiles, profiling/common.py:11)
+MISTRAL_7B = dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                  head_dim=128, intermediate_size=14336, vocab_size=32768, rms_norm_eps=1e-5,
+                  rope_parameters={"rope_type": "default", "rope_theta": 1e6}, sliding_window=None,
+                  max_position_embeddings=32768 + 1024, tie_word_embeddings=False)
+
+
+def build_random_mistral(seed: int = 0, dtype=torch.float16, device="cuda", nested: bool = True,
+                         **overrides) -> MistralForCausalLM:
+    """Random-init Mistral-shaped model (weights N(0, 0.02^2), RMSNorm weights 1) whose decoder
+    linears are quantised to bitsandbytes NF4 on the device (blocksize 64, double-quantised scales
+    with blocksize 256 when ``nested``). Embedding and lm_head stay dense in ``dtype``."""
+    cfg = MistralConfig(**{**MISTRAL_7B, **overrides})
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = MistralForCausalLM(cfg)
+    model.to(dtype)
+    model.eval()
+    quantize_model_linears(model.model, nested=nested)
+    torch.cuda.empty_cache()
+    return model
+
+
+class DecodeEngine:
+    """Static-cache, graph-captured greedy decode for a fixed batch size."""
+
+    def __init__(self, model: MistralForCausalLM, batch: int, max_len: int):
+        cfg = model.config
+        self.model = model
+        self.B, self.S = batch, max_len
+        self.L = cfg.num_hidden_layers
+        self.H, self.KVH = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.H
+        self.scale = self.D ** -0.5
+        p = next(model.parameters())
+        self.device, self.dtype = p.device, model.model.embed_tokens.weight.dtype
+        self.w = []
+        for layer in model.model.layers:
+            at, mlp = layer.self_attn, layer.mlp
+            self.w.append({n: NF4Weight(m.weight) for n, m in (
+                ("q", at.q_proj), ("k", at.k_proj), ("v", at.v_proj), ("o", at.o_proj),
+                ("gate", mlp.gate_proj), ("up", mlp.up_proj), ("down", mlp.down_proj))})
+        kv_shape = (self.L, batch, self.KVH, max_len, self.D)
+        self.k_cache = torch.zeros(kv_shape, dtype=self.dtype, device=self.device)
+        self.v_cache = torch.zeros(kv_shape, dtype=self.dtype, device=self.device)
+        self.ids = torch.zeros(batch, dtype=torch.long, device=self.device)      # input token per sequence
+        self.pos = torch.zeros(batch, dtype=torch.long, device=self.device)      # its position
+        self.next_ids = torch.zeros(batch, dtype=torch.long, device=self.device)
+        self.logits = torch.zeros(batch, cfg.vocab_size, dtype=self.dtype, device=self.device)  # last step's
+        self.bidx = torch.arange(batch, device=self.device)
+        self.graph = None
+        self.stream = torch.cuda.Stream(self.device)
+
+    # ----------------------------------------------------------------------------- one step
+    @torch.inference_mode()
+    def _step(self):
+        """Consume ``ids`` at ``pos``, write the step's K/V, produce ``next_ids``, advance ``pos``."""
+        m = self.model.model
+        B, H, KVH, D = self.B, self.H, self.KVH, self.D
+        h = m.embed_tokens(self.ids.view(B, 1))                      # [B, 1, hidden]
+        cos, sin = m.rotary_emb(h, self.pos.view(B, 1))
+        seqlens = (self.pos + 1).to(torch.int32)
+        for i, layer in enumerate(m.layers):
+            w = self.w[i]
+            r = h
+            x = layer.input_layernorm(h)
+            q = w["q"].matmul(x).view(B, 1, H, D).transpose(1, 2)
+            k = w["k"].matmul(x).view(B, 1, KVH, D).transpose(1, 2)
+            v = w["v"].matmul(x).view(B, 1, KVH, D).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            self.k_cache[i][self.bidx, :, self.pos] = k[:, :, 0]
+            self.v_cache[i][self.bidx, :, self.pos] = v[:, :, 0]
+            a = decode_attention(q, self.k_cache[i], self.v_cache[i], self.scale, seqlens=seqlens)
+            h = r + w["o"].matmul(a.reshape(B, 1, H * D))
+            r = h
+            x = layer.post_attention_layernorm(h)
+            g = w["gate"].matmul(x)
+            u = w["up"].matmul(x)
+            h = r + w["down"].matmul(layer.mlp.act_fn(g) * u)
+        logits = self.model.lm_head(m.norm(h))                       # [B, 1, vocab]
+        self.logits.copy_(logits[:, -1])
+        self.next_ids.copy_(logits[:, -1].argmax(-1))
+        self.ids.copy_(self.next_ids)
+        self.pos.add_(1)
+
+    def capture(self):
+        """Warm up (allocates every workspace on the capture stream) and capture one step."""
+        saved = (self.ids.clone(), self.pos.clone(), self.next_ids.clone())
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):
+                self._step()
+                self.ids.copy_(saved[0]); self.pos.copy_(saved[1])
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._step()
+        self.ids.copy_(saved[0]); self.pos.copy_(saved[1]); self.next_ids.copy_(saved[2])
+        torch.cuda.synchronize(self.device)
+
+    def step(self):
+        """One decode step on the current stream (graph replay once captured)."""
+        if self.graph is None:
+            self._step()
+        else:
+            self.graph.replay()
+        return self.next_ids
+
+    # ----------------------------------------------------------------------------- prefill / generate
+    @torch.inference_mode()
+    def prefill(self, prompt_ids: torch.Tensor) -> torch.Tensor:
+        """Run the prompts [B, P] through the HF forward, copy their K/V into the static cache and
+        set up the first decode input. Returns the first generated token per sequence."""
+        B, P = prompt_ids.shape
+        assert B == self.B and P < self.S, (prompt_ids.shape, self.B, self.S)
+        past = DynamicCache()
+        out = self.model(input_ids=prompt_ids.to(self.device), past_key_values=past, use_cache=True,
+                         logits_to_keep=1)
+        for i in range(self.L):
+            self.k_cache[i, :, :, :P] = past.layers[i].keys
+            self.v_cache[i, :, :, :P] = past.layers[i].values
+        first = out.logits[:, -1].argmax(-1)
+        self.ids.copy_(first)
+        self.next_ids.copy_(first)
+        self.pos.fill_(P)
+        return first
+
+    def fill_random_cache(self, context: int, seed: int = 0):
+        """Fill the first ``context`` cache slots with seeded N(0,1) K/V (long-context throughput runs)
+        and set up decode from position ``context``."""
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        for i in range(self.L):
+            self.k_cache[i, :, :, :context].normal_(generator=g)
+            self.v_cache[i, :, :, :context].normal_(generator=g)
+        self.pos.fill_(context)
+        self.ids.random_(0, self.model.config.vocab_size, generator=g)
+
+    @torch.inference_mode()
+    def teacher_forced(self, prompt_ids: torch.Tensor, tokens: torch.Tensor):
+        """Decode consuming the given tokens [B, T] (instead of our own argmax): returns our argmax
+        and logits (float) for steps 1..T-1, i.e. the prediction after consuming tokens[:, t-1]."""
+        self.prefill(prompt_ids)
+        if self.graph is None:
+            self.capture()
+        preds, logits = [], []
+        for t in range(1, tokens.shape[1]):
+            self.ids.copy_(tokens[:, t - 1])
+            preds.append(self.step().clone())
+            logits.append(self.logits.float())
+        return torch.stack(preds, 1), torch.stack(logits, 1)
+
+    @torch.inference_mode()
+    def generate(self, prompt_ids: torch.Tensor, new_tokens: int) -> torch.Tensor:
+        """Greedy decode: [B, P] prompts -> [B, new_tokens] generated ids (first from prefill)."""
+        out = [self.prefill(prompt_ids)]
+        if self.graph is None:
+            self.capture()
+        for _ in range(new_tokens - 1):
+            out.append(self.step().clone())
+        return torch.stack(out, dim=1)
+
+
+@torch.inference_mode()
+def hf_greedy(model, prompt_ids: torch.Tensor, new_tokens: int, return_logits: bool = False):
+    """The reference's greedy loop (``profiling/04_compare.py:21-31``) through the HF forward with a
+    ``DynamicCache``: whatever forward the model's modules currently have (stock or patched)."""
+    past = DynamicCache()
+    out = model(input_ids=prompt_ids, past_key_values=past, use_cache=True, logits_to_keep=1)
+    nxt = out.logits[:, -1:].argmax(-1)
+    toks, logits = [nxt], [out.logits[:, -1].float()]
+    for _ in range(new_tokens - 1):
+        out = model(input_ids=nxt, past_key_values=past, use_cache=True)
+        nxt = out.logits[:, -1:].argmax(-1)
+        toks.append(nxt)
+        if return_logits:
+            logits.append(out.logits[:, -1].float())
+    toks = torch.cat(toks, dim=1)
+    return (toks, torch.stack(logits, 1)) if return_logits else toks
