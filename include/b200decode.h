@@ -151,6 +151,21 @@ int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h,
                    void* workspace, size_t workspace_bytes,
                    void* out, int64_t so_b, int64_t so_h, int out_dtype, void* stream);
 
+/* b2d_gqa_decode without a caller workspace (no counterpart in the reference). For callers that
+ * cannot allocate device memory themselves -- a serving process whose allocator owns the whole device
+ * budget, or a plugin inside another framework's memory pool that must not cudaMalloc behind its
+ * back -- the split partials go to a static 8 MiB device array in the library (held by every GPU
+ * that loads it until exit). The function allocates nothing. Needs B*H*nsplit*(D+2)*4 bytes <= 8 MiB,
+ * else returns B2D_ERR_WORKSPACE with the sizes in b2d_last_cuda_error(). The first call on a device
+ * looks the array's address up once (make it before any stream capture). All calls on a device share
+ * the array: calls that overlap on the GPU race. Other arguments as b2d_gqa_decode. */
+int b2d_gqa_decode_noalloc(const void* q, int64_t sq_b, int64_t sq_h,
+                           const void* k, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                           const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                           const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                           float scale, int nsplit, int chunk, int dtype,
+                           void* out, int64_t so_b, int64_t so_h, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,9 @@ SIGNATURES = {
     "b2d_gqa_decode": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                               _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                               _p, _i64, _i64, _i32, _p]),
+    "b2d_gqa_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                                      _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32,
+                                      _p, _i64, _i64, _i32, _p]),
 }
 
 _lib = None

@@ -17,6 +17,8 @@ void set_cuda_error(cudaError_t e) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+void set_error_text(const char* text) { std::snprintf(g_last_error, sizeof(g_last_error), "%s", text); }
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return B2D_OK;

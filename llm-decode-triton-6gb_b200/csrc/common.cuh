@@ -13,6 +13,7 @@ namespace b2d {
 
 // ------------------------------------------------------------------ status helpers
 void set_cuda_error(cudaError_t e);
+void set_error_text(const char* text);    // message returned by b2d_last_cuda_error()
 int launch_status();                      // cudaGetLastError -> B2D_OK / B2D_ERR_LAUNCH
 
 struct DeviceInfo {

@@ -18,6 +18,8 @@
 //   No shared-memory staging for K/V: 16-byte global loads straight into fragment registers, one
 //   tile prefetched ahead. Warps of a CTA take interleaved tiles and merge through shared memory.
 // Workspace per (b, h, split): unnormalised O[D] (fp32) and (m, l) with m in the log2 domain.
+#include <cstdio>
+
 #include "common.cuh"
 
 namespace b2d {
@@ -441,4 +443,76 @@ extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((st = launch_partial(a, D, dtype, s)) != B2D_OK) return st;
   return launch_combine(a, D, out_dtype, s, true);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant of b2d_gqa_decode.
+//
+// Some callers cannot allocate device memory for the split-K partials: a serving process whose
+// allocator reserved the whole device budget up front and accounts for every byte, or a plugin that
+// lives inside another framework's memory pool and must not call cudaMalloc behind its back (a
+// cudaMalloc there can also stall the device while the host waits). For them the partials live in
+// this file-scope array instead of a caller workspace. Every GPU that loads the library holds the
+// array until the process exits. Nothing in it needs to start at zero (each call writes every
+// partial it later reads), but all calls on a device share it and keep the last call's contents, so
+// two calls that overlap on the GPU (different streams, no ordering between them) race.
+static constexpr size_t kGqaNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
+static __device__ __align__(256) uint8_t b2d_gqa_noalloc_scratch[kGqaNoAllocScratchBytes];
+
+namespace {
+void* g_noalloc_scratch_ptr[64] = {nullptr};   // device address of the array, per device
+}
+
+extern "C" int b2d_gqa_decode_noalloc(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b,
+                                      int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h,
+                                      int64_t sv_s, const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                                      float scale, int nsplit, int chunk, int dtype, void* out, int64_t so_b,
+                                      int64_t so_h, int out_dtype, void* stream) {
+  int st = check_attn(B, H, KVH, S, D, dtype);
+  if (st != B2D_OK) return st;
+  if (B == 0 || H == 0) return B2D_OK;
+  if (S == 0) return B2D_ERR_SHAPE;
+  DeviceInfo di;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  // the same split choice as b2d_gqa_decode, resolved here to size the scratch
+  if (nsplit <= 0 && chunk <= 0) {
+    nsplit = b2d_gqa_default_splits(B, KVH, S);
+    chunk = default_chunk(S, nsplit);
+    nsplit = (S + chunk - 1) / chunk;
+  } else if (chunk <= 0) {
+    chunk = default_chunk(S, nsplit);
+  } else if (nsplit <= 0) {
+    nsplit = (S + chunk - 1) / chunk;
+  }
+  const size_t need = b2d_gqa_workspace_bytes(B, H, nsplit, D);
+  if (need > kGqaNoAllocScratchBytes) {
+    char msg[200];
+    std::snprintf(msg, sizeof(msg),
+                  "b2d_gqa_decode_noalloc: %zu bytes of split partials needed (B=%d H=%d nsplit=%d D=%d), "
+                  "static scratch holds %zu; use fewer splits or b2d_gqa_decode with a workspace",
+                  need, B, H, nsplit, D, kGqaNoAllocScratchBytes);
+    set_error_text(msg);
+    return B2D_ERR_WORKSPACE;
+  }
+  // The host sees only a stand-in for the array's name; the kernels need its device address. The
+  // first call on each device (with that device current) looks it up once; make that first call
+  // before any stream capture.
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    if (e != cudaSuccess) set_cuda_error(e);
+    return B2D_ERR_DEVICE;
+  }
+  if (!g_noalloc_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, b2d_gqa_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_cuda_error(e);
+      return B2D_ERR_DEVICE;
+    }
+    g_noalloc_scratch_ptr[dev] = p;
+  }
+  return b2d_gqa_decode(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
+                        nsplit, chunk, dtype, g_noalloc_scratch_ptr[dev], kGqaNoAllocScratchBytes, out, so_b, so_h,
+                        out_dtype, stream);
 }
