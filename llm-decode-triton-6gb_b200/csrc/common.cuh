@@ -109,6 +109,20 @@ __device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
   return r;
 }
 
+// Asynchronous global -> shared copies (completion tracked per thread with commit/wait groups).
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
 // Device-scope acquire-release atomic add (cheaper than a sequentially consistent fence + atomic):
 // writes made before it by this thread, or by threads it synchronised with through a barrier, are
 // visible to whoever observes the new value; reads after it see what earlier releasers published.

@@ -227,6 +227,76 @@ __device__ __forceinline__ int cta_begin(int c, int total, int grid) { return c 
 // CTA whose slice contains unit p: the largest c with floor(c*total/grid) <= p.
 __device__ __forceinline__ int cta_of(int p, int total, int grid) { return ((p + 1) * grid - 1) / total; }
 
+// Combine the per-warp partials of the row groups this CTA touched: warp i handles the i-th group
+// (lanes own their fragment positions); its contributing warps are the contiguous range holding the
+// group's units. Groups shared with neighbouring CTAs go through the workspace (see below).
+template <typename OT, int RT, int NT, int NW>
+__device__ __forceinline__ void combine_cta(const GemmArgs& a, const float* slots, const int* s_wa, const int* s_wb,
+                                            const int* s_fg, int A, int B, int cta, int warp, int lane, int g,
+                                            int tq) {
+  constexpr int E = RT * NT * 128;
+  const int grid = gridDim.x, upg = a.upg;
+  if (A >= B) return;
+  const int gA = A / upg, gB = (B - 1) / upg;
+  const int span = B - A;
+  for (int grp = gA + warp; grp <= gB; grp += NW) {
+    const int lo = max(grp * upg, A), hi = min((grp + 1) * upg, B);   // this CTA's units of grp
+    const bool shared = grp * upg < A || (grp + 1) * upg > B;          // other CTAs hold the rest
+    const int w_lo = ((lo - A + 1) * NW - 1) / span, w_hi = ((hi - 1 - A + 1) * NW - 1) / span;
+    if (!shared && w_lo == w_hi) continue;                            // one warp stored it in full
+    float v[RT][NT][4];
+    zero_acc(v);
+    for (int w = w_lo; w <= w_hi; ++w) {
+      if (s_wa[w] >= s_wb[w]) continue;   // a warp without units (CTA slice shorter than NW)
+      const float* s = slots + (w * 2 + (grp == s_fg[w] ? 0 : 1)) * E + lane * 4;
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 q = *reinterpret_cast<const float4*>(s + (rt * NT + nt) * 128);
+          v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
+        }
+    }
+    if (!shared) {
+      store_group<OT, RT, NT>(a, grp, v, g, tq);
+      continue;
+    }
+    // Shared with neighbouring CTAs: publish this CTA's partial; the last arriver adds all partials
+    // in CTA order. The lanes' stores are ordered before lane 0's release by the warp barrier; lane
+    // 0's acquire (and the barrier after it) orders the last arriver's reads after every partial.
+    float* mine = a.partials + (static_cast<int64_t>(cta) * 2 + (grp == gA ? 0 : 1)) * E + lane * 4;
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        __stcg(reinterpret_cast<float4*>(mine + (rt * NT + nt) * 128),
+               make_float4(v[rt][nt][0], v[rt][nt][1], v[rt][nt][2], v[rt][nt][3]));
+    __syncwarp();
+    const int c_lo = cta_of(grp * upg, a.total, grid), c_hi = cta_of((grp + 1) * upg - 1, a.total, grid);
+    int last = 0;
+    if (lane == 0 && atomic_add_acq_rel_gpu(a.counters + grp, 1) == c_hi - c_lo) {
+      last = 1;
+      a.counters[grp] = 0;   // every contributor has arrived: reset for the next launch
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    if (!last) continue;
+    zero_acc(v);
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const int cfirst = cta_begin(c, a.total, grid) / upg;
+      const float* s = a.partials + (static_cast<int64_t>(c) * 2 + (grp == cfirst ? 0 : 1)) * E + lane * 4;
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 q = __ldcg(reinterpret_cast<const float4*>(s + (rt * NT + nt) * 128));
+          v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
+        }
+    }
+    store_group<OT, RT, NT>(a, grp, v, g, tq);
+  }
+}
+
 template <typename T, typename OT, int RT, int NT, int CB, bool NESTED, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs a) {
   constexpr int E = RT * NT * 128;  // fp32 values of one group partial, in fragment order
@@ -234,7 +304,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
   const uint8_t* lut = smem;
   float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);
   float* slots = code2_s + 256;  // [warps][2][E]
-  __shared__ int s_wa[NW], s_wb[NW], s_fg[NW], s_lg[NW];
+  __shared__ int s_wa[NW], s_wb[NW], s_fg[NW];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
@@ -250,7 +320,6 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
     s_wa[warp] = wa;
     s_wb[warp] = wb;
     s_fg[warp] = first_grp;
-    s_lg[warp] = wb > wa ? (wb - 1) / upg : -1;
   }
 
   // table inputs first, then the first unit's weights, all in flight while the table is built
@@ -320,67 +389,208 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
   }
   __syncthreads();
 
-  // ---- combine: warp i handles the i-th row group this CTA touched (lanes own their fragment
-  // positions). Its contributing warps are the contiguous range holding the group's units.
-  if (A >= B) return;
-  const int gA = A / upg, gB = (B - 1) / upg;
-  const int span = B - A;
-  for (int grp = gA + warp; grp <= gB; grp += NW) {
-    const int lo = max(grp * upg, A), hi = min((grp + 1) * upg, B);   // this CTA's units of grp
-    const bool shared = grp * upg < A || (grp + 1) * upg > B;          // other CTAs hold the rest
-    const int w_lo = ((lo - A + 1) * NW - 1) / span, w_hi = ((hi - 1 - A + 1) * NW - 1) / span;
-    if (!shared && w_lo == w_hi) continue;                            // one warp stored it in full
-    float v[RT][NT][4];
-    zero_acc(v);
-    for (int w = w_lo; w <= w_hi; ++w) {
-      if (s_wa[w] >= s_wb[w]) continue;   // a warp without units (CTA slice shorter than NW)
-      const float* s = slots + (w * 2 + (grp == s_fg[w] ? 0 : 1)) * E + lane * 4;
+  combine_cta<OT, RT, NT, NW>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
+}
+
+// ------------------------------------------------------------------------------------------
+// Pipelined variant for 32-row groups and 4-block units (the common M <= 8 decode shapes): each warp
+// streams its units through a private ring of R shared-memory stages filled by 16-byte cp.async
+// copies (8 lanes per 128-byte row segment, so one copy instruction moves 4 whole rows), with the
+// per-row scales riding in the same stage. R-1 units per warp are in flight while one is computed,
+// and no registers hold them. Inside a stage, the 16-byte chunk c of row r sits at chunk
+// c ^ 2*(r & 3): the fragment reads (8 bytes per lane, 4 rows x 2 chunks per half-warp) then hit 32
+// distinct banks without padding.
+constexpr int kStageW = 32 * 128;                // weights of one unit: 32 rows x 4 blocks x 32 B
+constexpr int kStageBytes = kStageW + 32 * 16;   // + scales, 16 B per row
+
+__device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (2 * (r & 3))) << 4); }
+
+template <bool NESTED>
+__device__ __forceinline__ void issue_unit(uint32_t st, const GemmArgs& a, int grp, int unit, int lane) {
+  const int64_t row0 = static_cast<int64_t>(grp) * 32;
+  const int c = lane & 7;
 #pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float4 q = *reinterpret_cast<const float4*>(s + (rt * NT + nt) * 128);
-          v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
-        }
-    }
-    if (!shared) {
-      store_group<OT, RT, NT>(a, grp, v, g, tq);
-      continue;
-    }
-    // Shared with neighbouring CTAs: publish this CTA's partial; the last arriver adds all partials
-    // in CTA order. The lanes' stores are ordered before lane 0's release by the warp barrier; lane
-    // 0's acquire (and the barrier after it) orders the last arriver's reads after every partial.
-    float* mine = a.partials + (static_cast<int64_t>(cta) * 2 + (grp == gA ? 0 : 1)) * E + lane * 4;
-#pragma unroll
-    for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        __stcg(reinterpret_cast<float4*>(mine + (rt * NT + nt) * 128),
-               make_float4(v[rt][nt][0], v[rt][nt][1], v[rt][nt][2], v[rt][nt][3]));
-    __syncwarp();
-    const int c_lo = cta_of(grp * upg, a.total, grid), c_hi = cta_of((grp + 1) * upg - 1, a.total, grid);
-    int last = 0;
-    if (lane == 0 && atomic_add_acq_rel_gpu(a.counters + grp, 1) == c_hi - c_lo) {
-      last = 1;
-      a.counters[grp] = 0;   // every contributor has arrived: reset for the next launch
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    __syncwarp();
-    if (!last) continue;
-    zero_acc(v);
-    for (int c = c_lo; c <= c_hi; ++c) {
-      const int cfirst = cta_begin(c, a.total, grid) / upg;
-      const float* s = a.partials + (static_cast<int64_t>(c) * 2 + (grp == cfirst ? 0 : 1)) * E + lane * 4;
-#pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float4 q = __ldcg(reinterpret_cast<const float4*>(s + (rt * NT + nt) * 128));
-          v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
-        }
-    }
-    store_group<OT, RT, NT>(a, grp, v, g, tq);
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    cp_async16(st + swz(r, c), a.w.packed + (row0 + r) * a.w.ld_packed + unit * 128 + c * 16);
   }
+  const int64_t row = row0 + lane;
+  const int64_t bi = row * a.w.ld_absmax + static_cast<int64_t>(unit) * 4;
+  if (NESTED) {
+    // a unit never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
+    cp_async4(st + kStageW + lane * 16, static_cast<const uint8_t*>(a.w.absmax) + bi);
+    cp_async4(st + kStageW + lane * 16 + 4,
+              a.w.absmax2 + ((a.w.gblk_base + row * a.w.gblk_row_stride + unit * 4) >> 8));
+  } else {
+    cp_async16(st + kStageW + lane * 16, static_cast<const float*>(a.w.absmax) + bi);
+  }
+}
+
+// One staged unit for a warp: 2 row tiles x 4 blocks. xv holds the activations of the unit's first
+// block on entry and of the next unit's first block on exit (when there is a next unit).
+template <typename T, int NT, bool NESTED>
+__device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmArgs& a, int unit, bool have_next,
+                                               uint4 (&xv)[NT][2], float (&acc)[2][NT][4], const uint8_t* lut,
+                                               uint32_t lane4, const float* code2_s, int g, int tq) {
+  float sc[2][2][4];
+#pragma unroll
+  for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint8_t* sp = stage + kStageW + (rt * 16 + h * 8 + g) * 16;
+      if (NESTED) {
+        const uint32_t q4 = *reinterpret_cast<const uint32_t*>(sp);
+        const float a2 = *reinterpret_cast<const float*>(sp + 4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[(q4 >> (8 * j)) & 0xFF], a2), a.w.offset);
+      } else {
+        const float4 v = *reinterpret_cast<const float4*>(sp);
+        sc[rt][h][0] = v.x; sc[rt][h][1] = v.y; sc[rt][h][2] = v.z; sc[rt][h][3] = v.w;
+      }
+    }
+  const int next_blk = (unit + 1) * 4 < (a.K >> 6) ? (unit + 1) * 4 : 0;   // next unit may open a new group
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 xn[NT][2];
+    if (j < 3) load_x<T, NT>(xn, a, unit * 4 + j + 1, g, tq);
+    else if (have_next) load_x<T, NT>(xn, a, next_blk, g, tq);
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt) {
+      const int r = rt * 16 + g;
+      const int cc = 2 * j + (tq >> 1), off = (tq & 1) * 8;
+      const uint2 wg = *reinterpret_cast<const uint2*>(stage + swz(r, cc) + off);
+      const uint2 wh = *reinterpret_cast<const uint2*>(stage + swz(r + 8, cc) + off);
+      float c[NT][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const uint32_t w0 = (s < 2) ? wg.x : wg.y;
+        const uint32_t w1 = (s < 2) ? wh.x : wh.y;
+        const uint32_t sel0 = (s & 1) ? 0x5524u : 0x5504u;
+        const uint32_t sel1 = (s & 1) ? 0x5534u : 0x5514u;
+        const uint32_t a0 = lut_lookup(lut, w0, lane4, sel0);
+        const uint32_t a2 = lut_lookup(lut, w0, lane4, sel1);
+        const uint32_t a1 = lut_lookup(lut, w1, lane4, sel0);
+        const uint32_t a3 = lut_lookup(lut, w1, lane4, sel1);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[nt][0]);
+          if (s == 0) Mma<T>::run0(c[nt], a0, a1, a2, a3, xw[0], xw[1]);
+          else Mma<T>::run(c[nt], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[rt][nt][0] = fmaf(sc[rt][0][j], c[nt][0], acc[rt][nt][0]);
+        acc[rt][nt][1] = fmaf(sc[rt][0][j], c[nt][1], acc[rt][nt][1]);
+        acc[rt][nt][2] = fmaf(sc[rt][1][j], c[nt][2], acc[rt][nt][2]);
+        acc[rt][nt][3] = fmaf(sc[rt][1][j], c[nt][3], acc[rt][nt][3]);
+      }
+    }
+    if (j < 3 || have_next) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) { xv[nt][0] = xn[nt][0]; xv[nt][1] = xn[nt][1]; }
+    }
+  }
+}
+
+template <int NW, int R, int NT>
+constexpr size_t pipe_smem_bytes() {
+  return kLutBytes + kCode2Bytes + static_cast<size_t>(NW) * 2 * (2 * NT * 128) * 4 +
+         static_cast<size_t>(NW) * R * kStageBytes;
+}
+
+template <typename T, typename OT, int NT, bool NESTED, int NW, int R>
+__global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArgs a) {
+  constexpr int RT = 2;
+  constexpr int E = RT * NT * 128;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint8_t* lut = smem;
+  float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);
+  float* slots = code2_s + 256;                                       // [NW][2][E]
+  uint8_t* rings = reinterpret_cast<uint8_t*>(slots + NW * 2 * E);   // [NW][R][kStageBytes]
+  __shared__ int s_wa[NW], s_wb[NW], s_fg[NW];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+  const int grid = gridDim.x, cta = blockIdx.x;
+  const int A = cta_begin(cta, a.total, grid), B = cta_begin(cta + 1, a.total, grid);
+  const int wa = A + warp * (B - A) / NW, wb = A + (warp + 1) * (B - A) / NW;
+  const int upg = a.upg;
+  const int first_grp = wa / upg;
+  if (lane == 0) { s_wa[warp] = wa; s_wb[warp] = wb; s_fg[warp] = first_grp; }
+
+  uint8_t* ring = rings + warp * (R * kStageBytes);
+  const uint32_t ring_s = smem_u32(ring);
+  const float my_code = __ldg(a.w.code + (lane & 15));
+  float my_code2 = 0.f;
+  if (NESTED && tid < 256) my_code2 = __ldg(a.w.code2 + tid);
+  // the first R-1 units are in flight while the table is built
+  int igrp = first_grp, iun = wa - first_grp * upg;
+#pragma unroll
+  for (int s = 0; s < R - 1; ++s) {
+    if (wa + s < wb) {
+      issue_unit<NESTED>(ring_s + s * kStageBytes, a, igrp, iun, lane);
+      if (++iun == upg) { iun = 0; ++igrp; }
+    }
+    cp_async_commit();
+  }
+  // table build: lane l of pass w computes entry 32w + l once and writes its 32 lane copies in a
+  // lane-rotated order, so every store instruction hits 32 distinct banks
+  for (int ew = warp; ew < 8; ew += NW) {
+    const int e = ew * 32 + lane;
+    const float hi = __shfl_sync(0xffffffffu, my_code, (e >> 4) & 15);
+    const float lo = __shfl_sync(0xffffffffu, my_code, e & 15);
+    const uint32_t val = Dt<T>::pack2(hi, lo);
+    uint32_t* entry = reinterpret_cast<uint32_t*>(smem + e * kLutEntryBytes);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) entry[(i + lane) & 31] = val;
+  }
+  if (NESTED)
+    for (int i = tid; i < 256; i += NW * 32) code2_s[i] = i == tid ? my_code2 : __ldg(a.w.code2 + i);
+  __syncthreads();
+
+  if (wa < wb) {
+    float acc[RT][NT][4];
+    zero_acc(acc);
+    int cgrp = first_grp, cun = wa - first_grp * upg;
+    uint4 xv[NT][2];
+    load_x<T, NT>(xv, a, cun * 4, g, tq);
+    auto park = [&](int grp) {   // a group this warp holds only part of: leave it for the combine
+      float* s = slots + (warp * 2 + (grp == first_grp ? 0 : 1)) * E + lane * 4;
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<float4*>(s + (rt * NT + nt) * 128) =
+              make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]);
+    };
+    for (int p = wa; p < wb; ++p) {
+      const int ip = p + R - 1;
+      if (ip < wb) {
+        issue_unit<NESTED>(ring_s + ((ip - wa) % R) * kStageBytes, a, igrp, iun, lane);
+        if (++iun == upg) { iun = 0; ++igrp; }
+      }
+      cp_async_commit();
+      cp_async_wait<R - 1>();
+      __syncwarp();
+      compute_staged<T, NT, NESTED>(ring + ((p - wa) % R) * kStageBytes, a, cun, p + 1 < wb, xv, acc, lut, lane4,
+                                    code2_s, g, tq);
+      __syncwarp();   // every lane is done with the stage before it is refilled
+      if (++cun == upg) {
+        if (cgrp * upg >= wa) store_group<OT, RT, NT>(a, cgrp, acc, g, tq);
+        else park(cgrp);
+        zero_acc(acc);
+        cun = 0;
+        ++cgrp;
+      }
+    }
+    if (cun != 0) park(cgrp);   // range ended inside a group
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  combine_cta<OT, RT, NT, NW>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -511,8 +721,34 @@ int launch_tc(const GemmArgs& a, int grid, cudaStream_t stream) {
   return launch_status();
 }
 
+#ifndef B2D_PIPE_NW
+#define B2D_PIPE_NW 8   // warps of the pipelined kernel
+#endif
+#ifndef B2D_PIPE_RING
+#define B2D_PIPE_RING 3   // stages per warp
+#endif
+
+template <typename T, typename OT, bool NESTED, int NW, int R>
+int launch_pipe(const GemmArgs& a, int grid, cudaStream_t stream) {
+  auto kern = nf4_gemm_pipe_kernel<T, OT, 1, NESTED, NW, R>;
+  constexpr size_t smem = pipe_smem_bytes<NW, R, 1>();
+  static bool configured[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B2D_ERR_DEVICE;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
+    configured[dev] = true;
+  }
+  kern<<<grid, NW * 32, smem, stream>>>(a);
+  return launch_status();
+}
+
 template <typename T, typename OT, int CB, bool NESTED>
 int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
+#ifndef B2D_PIPE_OFF
+  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, c.grid, s);
+#endif
   if (c.nt == 1)
     return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 10>(a, c.grid, s)
                      : launch_tc<T, OT, 1, 1, CB, NESTED, 16>(a, c.grid, s);
