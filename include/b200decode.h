@@ -45,6 +45,18 @@ enum {
 /* dtype codes for activations / outputs */
 enum { B2D_F16 = 0, B2D_BF16 = 1, B2D_F32 = 2 };
 
+/* Launch flags of the decode-step entry points (the *_ex / multi / glue calls):
+ *   B2D_LAUNCH_PDL      launch as a programmatic dependent of the previous kernel in the stream:
+ *                       the kernel may be scheduled while that kernel drains and waits (on the
+ *                       device) for its completion before touching stream-ordered data. Safe after
+ *                       any kernel; it only gains when the previous kernel is one of this library's.
+ *   B2D_STATIC_WEIGHTS  (NF4 GEMM) the weights are not written by the preceding kernels of the
+ *                       stream, so their prefetch may start before the previous kernel completes.
+ *   B2D_ATTN_FUSED_COMBINE  (attention) one launch: the last split CTA of each (sequence, KV head)
+ *                       to finish does the log-sum-exp combine (no second kernel). Applies when
+ *                       nsplit <= 64 and B*KVH <= 16384; otherwise the two-kernel path runs. */
+enum { B2D_LAUNCH_PDL = 1, B2D_STATIC_WEIGHTS = 2, B2D_ATTN_FUSED_COMBINE = 4 };
+
 const char* b2d_strerror(int status);
 /* Text of the last CUDA error seen by a launch in this thread ("" if none). */
 const char* b2d_last_cuda_error(void);
@@ -92,6 +104,41 @@ int b2d_nf4_gemm(const void* x, int64_t ldx,
                  void* y, int64_t ldy, int M, int N, int K, int dtype, int y_dtype,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* One weight of a segmented NF4 GEMM: the b2d_nf4_gemm weight arguments plus its row count and
+ * output. */
+typedef struct {
+  const uint8_t* packed;
+  int64_t ld_packed;
+  const void* absmax;
+  int64_t ld_absmax;
+  const float* code2;
+  const float* absmax2;
+  float offset;
+  int64_t gblk_base;
+  int64_t gblk_row_stride;
+  const float* code;
+  int N;
+  void* y;
+  int64_t ldy;
+} b2d_nf4_segment;
+
+enum { B2D_SEG_INDEPENDENT = 0, B2D_SEG_SILU_MUL = 1 };
+
+/* Several NF4 weights applied to the same x in ONE launch (no counterpart in the reference, which
+ * launches one kernel per projection; this fuses q/k/v and gate/up of a decoder layer).
+ *   mode B2D_SEG_INDEPENDENT: segs[i].y = x @ W_i^T for every segment (1 <= nseg <= 4, N_i % 32 == 0).
+ *   mode B2D_SEG_SILU_MUL:    nseg == 2, N_0 == N_1 (multiple of 16), y_dtype == dtype:
+ *                             segs[0].y = silu(x @ W_0^T) * (x @ W_1^T), every intermediate rounded to
+ *                             dtype as in a Mistral MLP (act_fn(gate_proj(x)) * up_proj(x)).
+ * 1 <= M <= 8. All segments share `nested` and segs[0].code (the 16-value NF4 codebook); per-segment
+ * scales (absmax/code2/absmax2/offset) are their own. Every segment's scales must allow 4-block
+ * loads: (K/64) % 4 == 0 and ld_absmax % 4 == 0; nested: gblk_base % 4 == 0 and gblk_row_stride % 4 == 0,
+ * plain: 16-byte aligned absmax. Workspace: b2d_nf4_gemm_workspace_bytes(M, sum of N_i, K).
+ * flags: B2D_LAUNCH_PDL | B2D_STATIC_WEIGHTS. */
+int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
+                       int M, int K, int dtype, int y_dtype, int mode, int flags,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* CUDA-core variant (fp32 FMAs, warp-shuffle reductions, no tensor cores) of b2d_nf4_gemm for
  * 1 <= M <= 8: same arguments and constraints, no workspace. Kept as the measured comparison
  * point for the tensor-core path. */
@@ -121,7 +168,9 @@ int b2d_nf4_double_quant(const float* absmax, int64_t n_blocks, const float* cod
  * strides in elements. Query head h reads KV head h / (H / KVH). seqlens: int32 [B] valid
  * keys per sequence (NULL = all S). Keys [split*chunk, (split+1)*chunk) form one split.
  * D in {64, 128}; G = H / KVH in 1..16; dtype F16 or BF16 for q, k, v; out_dtype = dtype or F32.
- * Workspace (fp32): acc [B, H, nsplit, D] followed by ml [B, H, nsplit, 2].
+ * Workspace: a 64 KiB region of int32 arrival counters (used by the single-launch combine), then
+ * fp32 acc [B, H, nsplit, D] and ml [B, H, nsplit, 2]. Zero-fill a new workspace once; launches leave
+ * the counters at zero, so one workspace serves any sequence of calls on one stream.
  * ================================================================================== */
 
 /* Split count the library picks for (B, KVH, S) on the current device (chunk = ceil(S/nsplit)
@@ -151,12 +200,59 @@ int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h,
                    void* workspace, size_t workspace_bytes,
                    void* out, int64_t so_b, int64_t so_h, int out_dtype, void* stream);
 
+/* b2d_gqa_decode with launch flags (B2D_LAUNCH_PDL: the partial kernel is launched as a programmatic
+ * dependent of the previous kernel in the stream). */
+int b2d_gqa_decode_ex(const void* q, int64_t sq_b, int64_t sq_h,
+                      const void* k, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                      const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                      const int32_t* seqlens, int B, int H, int KVH, int S, int D,
+                      float scale, int nsplit, int chunk, int dtype,
+                      void* workspace, size_t workspace_bytes,
+                      void* out, int64_t so_b, int64_t so_h, int out_dtype, int flags, void* stream);
+
+/* ================================================================ decode-step glue
+ * The small per-layer operations of a Mistral decoder layer around the two hot paths, as kernels
+ * that take B2D_LAUNCH_PDL (no counterpart in the reference, which runs these as separate torch ops:
+ * transformers' MistralRMSNorm, apply_rotary_pos_emb, DynamicCache.update, SiLU and the residual
+ * adds). dtype F16 or BF16; every intermediate is rounded to dtype where the torch code rounds.
+ * ================================================================================== */
+
+/* Residual add + RMSNorm over rows of width D (M rows, D % 8 == 0, D <= 8192):
+ *   h = residual + x (rounded; x may be NULL: h = residual), written back into residual;
+ *   out = round(weight * round(h * rsqrt(mean(h^2) + eps)))   (MistralRMSNorm, fp32 statistics).
+ * With B2D_LAUNCH_PDL the norm weight is read before the previous kernel completes: it must not be
+ * written by that kernel. */
+int b2d_add_rmsnorm(const void* x, int64_t ldx, void* residual, int64_t ldr, const void* weight, float eps,
+                    void* out, int64_t ldo, int M, int D, int dtype, int flags, void* stream);
+
+/* Rotary embedding of one new token per sequence plus the KV-cache append.
+ * q: [B, H*D] (row stride ldq), k, v: [B, KVH*D] (ldk, ldv), the projection outputs;
+ * pos: int64 [B], the token's position; cos, sin: [S_max, D] tables (row stride ld_cs) holding the
+ * model's rotary values in dtype (HF rotary_emb output for positions 0..S_max-1).
+ *   q_out[b, h, :]             = q*cos + rotate_half(q)*sin  (strides sqo_b, sqo_h; may alias q)
+ *   k_cache[b, kvh, pos[b], :] = k*cos + rotate_half(k)*sin  (strides skc_b, skc_h, skc_s)
+ *   v_cache[b, kvh, pos[b], :] = v                            (strides svc_b, svc_h, svc_s)
+ *   seqlens[b] = pos[b] + 1 (int32; seqlens may be NULL).
+ * A position outside [0, S_max) writes nothing for that sequence and sets seqlens[b] = 0.
+ * D % 4 == 0, D <= 256, H % KVH == 0. */
+int b2d_rope_kv_append(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                       const int64_t* pos, const void* cos, const void* sin, int64_t ld_cs,
+                       void* q_out, int64_t sqo_b, int64_t sqo_h,
+                       void* k_cache, int64_t skc_b, int64_t skc_h, int64_t skc_s,
+                       void* v_cache, int64_t svc_b, int64_t svc_h, int64_t svc_s,
+                       int32_t* seqlens, int B, int H, int KVH, int D, int S_max, int dtype, int flags,
+                       void* stream);
+
+/* out[m, n] = round(round(silu(gate[m, n])) * up[m, n]) for M rows of N (N % 8 == 0). */
+int b2d_silu_mul(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo,
+                 int M, int N, int dtype, int flags, void* stream);
+
 /* b2d_gqa_decode without a caller workspace (no counterpart in the reference). For callers that
  * cannot allocate device memory themselves -- a serving process whose allocator owns the whole device
  * budget, or a plugin inside another framework's memory pool that must not cudaMalloc behind its
  * back -- the split partials go to a static 8 MiB device array in the library (held by every GPU
- * that loads it until exit). The function allocates nothing. Needs B*H*nsplit*(D+2)*4 bytes <= 8 MiB,
- * else returns B2D_ERR_WORKSPACE with the sizes in b2d_last_cuda_error(). The first call on a device
+ * that loads it until exit). The function allocates nothing. Needs 64 KiB + B*H*nsplit*(D+2)*4 bytes
+ * <= 8 MiB, else returns B2D_ERR_WORKSPACE with the sizes in b2d_last_cuda_error(). The first call on a device
  * looks the array's address up once (make it before any stream capture). All calls on a device share
  * the array: calls that overlap on the GPU race. Other arguments as b2d_gqa_decode. */
 int b2d_gqa_decode_noalloc(const void* q, int64_t sq_b, int64_t sq_h,

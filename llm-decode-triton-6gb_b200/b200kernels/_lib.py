@@ -16,6 +16,17 @@ F16, BF16, F32 = 0, 1, 2
 
 _p, _i64, _i32, _f32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 
+LAUNCH_PDL, STATIC_WEIGHTS, ATTN_FUSED_COMBINE = 1, 2, 4   # launch flags
+SEG_INDEPENDENT, SEG_SILU_MUL = 0, 1         # b2d_nf4_gemm_multi modes
+
+
+class Nf4Segment(C.Structure):
+    """b2d_nf4_segment (include/b200decode.h)."""
+    _fields_ = [("packed", _p), ("ld_packed", _i64), ("absmax", _p), ("ld_absmax", _i64),
+                ("code2", _p), ("absmax2", _p), ("offset", _f32), ("gblk_base", _i64),
+                ("gblk_row_stride", _i64), ("code", _p), ("N", _i32), ("y", _p), ("ldy", _i64)]
+
+
 # name -> (restype, argtypes); mirrors include/b200decode.h
 SIGNATURES = {
     "b2d_strerror": (C.c_char_p, [_i32]),
@@ -39,6 +50,16 @@ SIGNATURES = {
     "b2d_gqa_decode": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                               _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                               _p, _i64, _i64, _i32, _p]),
+    "b2d_nf4_gemm_multi": (_i32, [_p, _i64, C.POINTER(Nf4Segment), _i32, _i32, _i32, _i32, _i32, _i32,
+                                  _i32, _i32, _p, _sz, _p]),
+    "b2d_gqa_decode_ex": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                                 _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
+                                 _p, _i64, _i64, _i32, _i32, _p]),
+    "b2d_add_rmsnorm": (_i32, [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i32, _i32, _i32, _i32, _p]),
+    "b2d_rope_kv_append": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64,
+                                  _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p,
+                                  _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
+    "b2d_silu_mul": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _p]),
     "b2d_gqa_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                       _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32,
                                       _p, _i64, _i64, _i32, _p]),

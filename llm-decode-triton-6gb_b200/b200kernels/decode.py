@@ -3,17 +3,18 @@
 The reference decodes through ``model(input_ids, past_key_values, use_cache=True)`` one token at a
 time (``profiling/common.py:80-85``, ``profiling/04_compare.py:21-31``); HF's ``DynamicCache`` grows
 the KV tensors with ``torch.cat`` every step and Python launches every kernel, so the step cannot be
-replayed as a CUDA graph. This engine keeps the HF modules for the small glue ops (embedding,
-RMSNorm, rotary embedding, SiLU, lm_head, argmax -- the same torch code as the stock path) and
-swaps the two hot paths for the B200 kernels:
+replayed as a CUDA graph. This engine decodes over a static KV cache ``[layers, B, KVH, S_max, D]``
+with per-sequence lengths and captures one whole decode step (32 layers) in a CUDA graph:
 
-* every NF4 linear (q/k/v/o/gate/up/down) -> ``NF4Weight.matmul`` (fused dequant + matmul);
-* attention -> ``decode_attention`` over a static KV cache ``[layers, B, KVH, S_max, D]`` with
-  per-sequence lengths,
+* every NF4 linear -> the fused dequant + matmul kernel; with ``fused=True`` q/k/v share one launch
+  and gate/up share one launch whose epilogue applies the SwiGLU;
+* attention -> ``decode_attention`` (split-K partial + log-sum-exp combine);
+* the glue ops (residual add + RMSNorm, rotary embedding + KV append) -> this library's kernels
+  (``fused=True``), every launch a programmatic dependent of the previous one; or the HF modules
+  themselves (``fused=False``). Embedding, lm_head and argmax stay torch ops.
 
-and captures one whole decode step (32 layers) in a CUDA graph. Prompts are prefilled through the
-HF forward (the reference's prefill path: SDPA, and dequant + library GEMM for the many-row
-linears); the prompt's K/V are then copied into the static cache.
+Prompts are prefilled through the HF forward (the reference's prefill path: SDPA, and dequant +
+library GEMM for the many-row linears); the prompt's K/V are then copied into the static cache.
 """
 from __future__ import annotations
 
@@ -22,9 +23,11 @@ from transformers import MistralConfig, MistralForCausalLM
 from transformers.cache_utils import DynamicCache
 from transformers.models.mistral.modeling_mistral import apply_rotary_pos_emb
 
+from . import _lib
 from .decode_attention import decode_attention
+from .glue import add_rmsnorm, rope_kv_append, silu_mul
 from .linear4bit import quantize_model_linears
-from .nf4_gemm import NF4Weight
+from .nf4_gemm import NF4Group, NF4Weight
 
 # Mistral-7B-v0.3 shape (the checkpoint the reference profiles, profiling/common.py:11)
 MISTRAL_7B = dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
@@ -51,9 +54,16 @@ def build_random_mistral(seed: int = 0, dtype=torch.float16, device="cuda", nest
 
 
 class DecodeEngine:
-    """Static-cache, graph-captured greedy decode for a fixed batch size."""
+    """Static-cache, graph-captured greedy decode for a fixed batch size.
 
-    def __init__(self, model: MistralForCausalLM, batch: int, max_len: int):
+    ``fused=True`` (default) runs every per-layer op on this library's kernels, 9 launches per layer
+    chained with programmatic dependent launch: add+RMSNorm, q/k/v in one NF4 launch, RoPE + KV
+    append, attention (partial + combine), o_proj, add+RMSNorm, gate/up in one launch with the SwiGLU
+    epilogue, down_proj (batch > 8: separate gate/up launches and a SiLU*mul kernel). ``fused=False``
+    keeps the HF modules for the glue ops (the same torch code as the stock path) around the two hot
+    kernels."""
+
+    def __init__(self, model: MistralForCausalLM, batch: int, max_len: int, fused: bool = True):
         cfg = model.config
         self.model = model
         self.B, self.S = batch, max_len
@@ -79,11 +89,86 @@ class DecodeEngine:
         self.bidx = torch.arange(batch, device=self.device)
         self.graph = None
         self.stream = torch.cuda.Stream(self.device)
+        self.fused = fused
+        if fused:
+            self._init_fused(cfg)
+
+    def _init_fused(self, cfg):
+        B, dev, dt = self.B, self.device, self.dtype
+        hid, inter = cfg.hidden_size, cfg.intermediate_size
+        self.eps = cfg.rms_norm_eps
+        self.pair = B <= NF4Group.MAX_M
+        self.groups = []
+        for w in self.w:
+            g = {"o": NF4Group([w["o"]]) if self.pair else None,
+                 "down": NF4Group([w["down"]]) if self.pair else None}
+            if self.pair:
+                g["qkv"] = NF4Group([w["q"], w["k"], w["v"]])
+                g["gateup"] = NF4Group([w["gate"], w["up"]], mode="silu_mul")
+            self.groups.append(g)
+        z = lambda *shape: torch.zeros(shape, dtype=dt, device=dev)
+        self.r = z(B, hid)                                   # residual stream
+        self.xn = z(B, hid)                                  # normalised activations
+        self.q = z(B, self.H * self.D)
+        self.k = z(B, self.KVH * self.D)
+        self.v = z(B, self.KVH * self.D)
+        self.attn = z(B, 1, self.H, self.D)
+        self.o_out = z(B, hid)
+        self.h_mlp = z(B, inter)
+        self.g_out = None if self.pair else z(B, inter)
+        self.down_out = z(B, hid)
+        self.seqlens = torch.zeros(B, dtype=torch.int32, device=dev)
+        # rotary tables for every cache position, computed by the model's own rotary module
+        pos = torch.arange(self.S, device=dev).view(1, -1)
+        cos, sin = self.model.model.rotary_emb(self.r.view(B, 1, hid)[:1], pos)
+        self.cos, self.sin = cos[0].to(dt).contiguous(), sin[0].to(dt).contiguous()
+
+    @torch.inference_mode()
+    def _step_fused(self):
+        m = self.model.model
+        B, H, KVH, D = self.B, self.H, self.KVH, self.D
+        PDL, STATIC = _lib.LAUNCH_PDL, _lib.LAUNCH_PDL | _lib.STATIC_WEIGHTS
+        torch.index_select(m.embed_tokens.weight, 0, self.ids, out=self.r)
+        x_in = None
+        for i, layer in enumerate(m.layers):
+            w, g = self.w[i], self.groups[i]
+            add_rmsnorm(self.r, layer.input_layernorm.weight, self.eps, self.xn, x=x_in, flags=PDL)
+            if self.pair:
+                g["qkv"].matmul(self.xn, [self.q, self.k, self.v], flags=STATIC)
+            else:
+                w["q"].matmul(self.xn, out=self.q); w["k"].matmul(self.xn, out=self.k); w["v"].matmul(self.xn, out=self.v)
+            q3 = self.q.view(B, H, D)
+            rope_kv_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, q3, self.k_cache[i], self.v_cache[i],
+                           self.seqlens, flags=PDL)
+            decode_attention(q3.view(B, H, 1, D), self.k_cache[i], self.v_cache[i], self.scale, seqlens=self.seqlens,
+                             out=self.attn, flags=PDL)
+            a2 = self.attn.view(B, H * D)
+            if self.pair:
+                g["o"].matmul(a2, [self.o_out], flags=STATIC)
+            else:
+                w["o"].matmul(a2, out=self.o_out)
+            add_rmsnorm(self.r, layer.post_attention_layernorm.weight, self.eps, self.xn, x=self.o_out, flags=PDL)
+            if self.pair:
+                g["gateup"].matmul(self.xn, [self.h_mlp], flags=STATIC)
+                g["down"].matmul(self.h_mlp, [self.down_out], flags=STATIC)
+            else:
+                w["gate"].matmul(self.xn, out=self.g_out); w["up"].matmul(self.xn, out=self.h_mlp)
+                silu_mul(self.g_out, self.h_mlp, out=self.h_mlp, flags=PDL)
+                w["down"].matmul(self.h_mlp, out=self.down_out)
+            x_in = self.down_out
+        add_rmsnorm(self.r, m.norm.weight, self.eps, self.xn, x=x_in, flags=PDL)
+        logits = self.model.lm_head(self.xn)                        # [B, vocab]
+        self.logits.copy_(logits)
+        torch.argmax(logits, -1, out=self.next_ids)
+        self.ids.copy_(self.next_ids)
+        self.pos.add_(1)
 
     # ----------------------------------------------------------------------------- one step
     @torch.inference_mode()
     def _step(self):
         """Consume ``ids`` at ``pos``, write the step's K/V, produce ``next_ids``, advance ``pos``."""
+        if self.fused:
+            return self._step_fused()
         m = self.model.model
         B, H, KVH, D = self.B, self.H, self.KVH, self.D
         h = m.embed_tokens(self.ids.view(B, 1))                      # [B, 1, hidden]

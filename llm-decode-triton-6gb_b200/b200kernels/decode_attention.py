@@ -29,7 +29,7 @@ def attention_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.index, stream.cuda_stream)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)   # counters start at zero
         _WS[key] = ws
     return ws
 
@@ -46,9 +46,10 @@ def plan_splits(B: int, KVH: int, S: int, chunk: int | None = None) -> tuple[int
 
 
 def decode_attention(q, k, v, scale=None, chunk=None, block_s=None, seqlens=None, out=None, workspace=None,
-                     out_dtype=None):
+                     out_dtype=None, flags=0):
     """q [B, H, 1, D], k/v [B, KVH, S, D] (fp16/bf16, last dim contiguous) -> [B, 1, H, D] in
-    ``out_dtype`` (q's dtype or torch.float32; default q's dtype)."""
+    ``out_dtype`` (q's dtype or torch.float32; default q's dtype). ``flags``: ``_lib.LAUNCH_PDL``
+    launches the partial kernel as a programmatic dependent of the previous kernel."""
     B, H, one, D = q.shape
     KVH, S = k.shape[1], k.shape[2]
     if one != 1:
@@ -76,11 +77,13 @@ def decode_attention(q, k, v, scale=None, chunk=None, block_s=None, seqlens=None
         if seqlens.dtype != torch.int32 or seqlens.device != q.device:
             seqlens = seqlens.to(device=q.device, dtype=torch.int32)
         seqlens = seqlens.contiguous()
-    _lib.call("b2d_gqa_decode",
-              q.data_ptr(), q.stride(0), q.stride(1),
-              k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
-              v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
-              _lib.ptr(seqlens), B, H, KVH, S, D, float(scale), nsplit, chunk, _lib.dtype_code(q.dtype),
-              ws.data_ptr(), ws.numel(), out.data_ptr(), out.stride(0), out.stride(2), _lib.dtype_code(out.dtype),
-              _lib.stream_ptr(q.device))
+    args = (q.data_ptr(), q.stride(0), q.stride(1),
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
+            _lib.ptr(seqlens), B, H, KVH, S, D, float(scale), nsplit, chunk, _lib.dtype_code(q.dtype),
+            ws.data_ptr(), ws.numel(), out.data_ptr(), out.stride(0), out.stride(2), _lib.dtype_code(out.dtype))
+    if flags:
+        _lib.call("b2d_gqa_decode_ex", *args, int(flags), _lib.stream_ptr(q.device))
+    else:
+        _lib.call("b2d_gqa_decode", *args, _lib.stream_ptr(q.device))
     return out

@@ -159,6 +159,62 @@ class NF4Weight:
         return n
 
 
+class NF4Group:
+    """Several NF4 weights applied to one activation in a single launch (``b2d_nf4_gemm_multi``;
+    no counterpart in the reference, which runs one kernel per projection).
+
+    ``mode="independent"``: ``outs[i] = x @ W_i^T`` (q/k/v of a decoder layer).
+    ``mode="silu_mul"``: two weights of equal shape, ``out = silu(x @ W_0^T) * (x @ W_1^T)`` with the
+    model-dtype rounding of a Mistral MLP (gate/up fused with the SwiGLU).
+    Up to ``MAX_M = 8`` rows. ``flags``: ``_lib.LAUNCH_PDL | _lib.STATIC_WEIGHTS``."""
+
+    MAX_M = 8
+
+    def __init__(self, weights: list, mode: str = "independent"):
+        assert 1 <= len(weights) <= 4 and mode in ("independent", "silu_mul"), (len(weights), mode)
+        w0 = weights[0]
+        for w in weights:
+            assert w.K == w0.K and w.nested == w0.nested, "segments must share K and the nested flag"
+            assert torch.equal(w.code, w0.code), "segments must share the NF4 codebook"
+        self.mode = _lib.SEG_SILU_MUL if mode == "silu_mul" else _lib.SEG_INDEPENDENT
+        if self.mode == _lib.SEG_SILU_MUL:
+            assert len(weights) == 2 and weights[0].N == weights[1].N
+        self.weights = list(weights)
+        self.K, self.nested = w0.K, w0.nested
+        self.Ns = [w.N for w in weights]
+        self.n_out = [weights[0].N] if self.mode == _lib.SEG_SILU_MUL else self.Ns
+        self._segs = (_lib.Nf4Segment * len(weights))()
+        for i, w in enumerate(weights):
+            sg = self._segs[i]
+            sg.packed, sg.ld_packed = _lib.ptr(w.packed), w.ld_packed
+            sg.absmax, sg.ld_absmax = _lib.ptr(w.absmax), w.ld_absmax
+            sg.code2, sg.absmax2, sg.offset = _lib.ptr(w.code2), _lib.ptr(w.absmax2), w.offset
+            sg.gblk_base, sg.gblk_row_stride = w.gblk_base, w.gblk_row_stride
+            sg.code, sg.N = _lib.ptr(w.code), w.N
+
+    @property
+    def nbytes(self) -> int:
+        return sum(w.nbytes for w in self.weights)
+
+    def matmul(self, x: torch.Tensor, outs: list | None = None, flags: int = 0) -> list:
+        """x [M, K] (row stride multiple of 8) -> list of outputs [M, N_i] (or one for silu_mul)."""
+        assert x.dim() == 2 and x.shape[1] == self.K and x.stride(1) == 1, tuple(x.shape)
+        M = x.shape[0]
+        if outs is None:
+            outs = [torch.empty((M, n), device=x.device, dtype=x.dtype) for n in self.n_out]
+        for i, o in enumerate(outs):
+            self._segs[i].y, self._segs[i].ldy = o.data_ptr(), o.stride(0)
+        if self.mode == _lib.SEG_SILU_MUL:
+            self._segs[1].y, self._segs[1].ldy = outs[0].data_ptr(), outs[0].stride(0)
+        nbytes = _lib.load().b2d_nf4_gemm_workspace_bytes(max(M, 1), sum(self.Ns), self.K)
+        ws = gemm_workspace(x.device, nbytes)
+        dt = _lib.dtype_code(x.dtype)
+        _lib.call("b2d_nf4_gemm_multi", x.data_ptr(), x.stride(0), self._segs, len(self.weights), int(self.nested),
+                  M, self.K, dt, _lib.dtype_code(outs[0].dtype), self.mode, flags, ws.data_ptr(), ws.numel(),
+                  _lib.stream_ptr(x.device))
+        return outs
+
+
 def dequantize(param, dtype=torch.float16) -> torch.Tensor:
     """Bit-exact dequant of a bitsandbytes-format NF4 parameter on the device."""
     return NF4Weight(param).dequantize(dtype)

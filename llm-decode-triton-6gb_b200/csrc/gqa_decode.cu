@@ -27,6 +27,11 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
+// Workspace layout: a fixed-size region of per-(sequence, KV head) arrival counters first (so calls
+// of any shape agree on where they live and always find them zero), then the split partials.
+constexpr size_t kAttnCounterBytes = 64 * 1024;
+constexpr int kMaxAttnCounters = static_cast<int>(kAttnCounterBytes / 4);
+constexpr int kMaxFusedSplits = 64;   // the in-kernel combine loops over the splits per element
 
 struct AttnArgs {
   const void* q; int64_t sq_b, sq_h;
@@ -39,7 +44,16 @@ struct AttnArgs {
   float* acc;   // [B*H*nsplit][D]
   float* ml;    // [B*H*nsplit][2]
   void* out; int64_t so_b, so_h;
+  int* counters;   // [B*KVH], zero between launches
+  int fused;       // 1: the last split CTA of each (b, kvh) combines and writes out
+  int out_f32;     // fused: out is fp32 (else the input dtype)
 };
+
+template <typename T>
+__device__ __forceinline__ void store_out(const AttnArgs& a, int b, int h, int d, float v) {
+  if (a.out_f32) static_cast<float*>(a.out)[b * a.so_b + h * a.so_h + d] = v;
+  else static_cast<T*>(a.out)[b * a.so_b + h * a.so_h + d] = Dt<T>::from_f32(v);
+}
 
 __device__ __forceinline__ int seqlen_of(const AttnArgs& a, int b) {
   if (!a.seqlens) return a.S;
@@ -82,12 +96,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
   __shared__ float s_o[kAttnWarps][ROWS][D];
   __shared__ float s_m[kAttnWarps][ROWS], s_l[kAttnWarps][ROWS];
 
+  pdl_wait();   // no-op unless launched as a programmatic dependent
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
   const int len = seqlen_of(a, b);
   const int t_begin = split * a.chunk;
-  if (t_begin >= len) return;   // this split holds no keys; the combine skips it
+  if (t_begin >= len) {   // this split holds no keys; the combine skips it
+    if (a.fused && split == 0)   // an empty sequence: its heads get zeros, as the combine kernel writes
+      for (int idx = threadIdx.x; idx < a.G * D; idx += kAttnWarps * 32)
+        store_out<T>(a, b, kvh * a.G + idx / D, idx % D, 0.f);
+    return;
+  }
   const int t_end = min(t_begin + a.chunk, len);
 
   // ---- Q fragments (rows = heads of this KV group), permuted head-dim order
@@ -233,6 +253,37 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
     }
   }
   pdl_launch_dependents();
+  if (!a.fused) return;
+
+  // ---- single-launch mode: the last of the sequence's valid splits to arrive combines them. The
+  // barrier orders every thread's partial stores before thread 0's release; thread 0's acquire (and
+  // the barrier after it) orders the reads below after every other split's partial.
+  __shared__ int s_last;
+  const int nvalid = min(a.nsplit, (len + a.chunk - 1) / a.chunk);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = a.counters + b * a.KVH + kvh;
+    const int last = atomic_add_acq_rel_gpu(ctr, 1) == nvalid - 1;
+    if (last) *ctr = 0;   // every split has arrived: reset for the next launch
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int64_t head0 = static_cast<int64_t>(b) * a.H + kvh * a.G;
+  for (int idx = threadIdx.x; idx < a.G * D; idx += kAttnWarps * 32) {
+    const int row = idx / D, d = idx - row * D;
+    const int64_t base = (head0 + row) * a.nsplit;
+    float mx = -INFINITY;
+    for (int i = 0; i < nvalid; ++i) mx = fmaxf(mx, __ldcg(a.ml + (base + i) * 2));
+    float num = 0.f, den = 0.f;
+    for (int i = 0; i < nvalid; ++i) {
+      const float m = __ldcg(a.ml + (base + i) * 2);
+      const float w = m == -INFINITY ? 0.f : exp2f(m - mx);
+      num += w * __ldcg(a.acc + (base + i) * D + d);
+      den += w * __ldcg(a.ml + (base + i) * 2 + 1);
+    }
+    store_out<T>(a, b, kvh * a.G + row, d, den > 0.f ? num / den : 0.f);
+  }
 }
 
 // One CTA per (b, h), one thread per head-dim element. OT: output dtype.
@@ -281,26 +332,26 @@ int fill_args(AttnArgs* a, const void* q, int64_t sq_b, int64_t sq_h, const void
   a->B = B; a->H = H; a->KVH = KVH; a->S = S; a->G = KVH ? H / KVH : 1;
   a->scale_log2 = scale * kLog2e;
   a->nsplit = nsplit; a->chunk = chunk;
-  a->acc = static_cast<float*>(const_cast<void*>(ws));
+  a->counters = static_cast<int*>(const_cast<void*>(ws));
+  a->acc = reinterpret_cast<float*>(static_cast<uint8_t*>(const_cast<void*>(ws)) + kAttnCounterBytes);
   a->ml = a->acc + static_cast<size_t>(B) * H * nsplit * D;
   return B2D_OK;
 }
 
 template <typename T, int D>
-int launch_partial_t(const AttnArgs& a, cudaStream_t s) {
-  dim3 grid(a.nsplit, a.KVH, a.B);
-  if (a.G > 8) gqa_partial_kernel<T, D, true><<<grid, kAttnWarps * 32, 0, s>>>(a);
-  else gqa_partial_kernel<T, D, false><<<grid, kAttnWarps * 32, 0, s>>>(a);
-  return launch_status();
+int launch_partial_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
+  const dim3 grid(a.nsplit, a.KVH, a.B);
+  if (a.G > 8) return launch_kernel(gqa_partial_kernel<T, D, true>, grid, dim3(kAttnWarps * 32), 0, s, pdl, a);
+  return launch_kernel(gqa_partial_kernel<T, D, false>, grid, dim3(kAttnWarps * 32), 0, s, pdl, a);
 }
 
-int launch_partial(const AttnArgs& a, int D, int dtype, cudaStream_t s) {
+int launch_partial(const AttnArgs& a, int D, int dtype, cudaStream_t s, bool pdl = false) {
   if (dtype == B2D_F16) {
-    if (D == 64) return launch_partial_t<__half, 64>(a, s);
-    return launch_partial_t<__half, 128>(a, s);
+    if (D == 64) return launch_partial_t<__half, 64>(a, s, pdl);
+    return launch_partial_t<__half, 128>(a, s, pdl);
   }
-  if (D == 64) return launch_partial_t<__nv_bfloat16, 64>(a, s);
-  return launch_partial_t<__nv_bfloat16, 128>(a, s);
+  if (D == 64) return launch_partial_t<__nv_bfloat16, 64>(a, s, pdl);
+  return launch_partial_t<__nv_bfloat16, 128>(a, s, pdl);
 }
 
 template <typename T, int D>
@@ -362,7 +413,7 @@ extern "C" int b2d_gqa_default_splits(int B, int KVH, int S) {
 
 extern "C" size_t b2d_gqa_workspace_bytes(int B, int H, int nsplit, int D) {
   if (B <= 0 || H <= 0 || nsplit <= 0 || D <= 0) return 0;
-  return static_cast<size_t>(B) * H * nsplit * (D + 2) * sizeof(float);
+  return kAttnCounterBytes + static_cast<size_t>(B) * H * nsplit * (D + 2) * sizeof(float);
 }
 
 static int default_chunk(int S, int nsplit) {
@@ -410,11 +461,11 @@ extern "C" int b2d_gqa_decode_combine(const int32_t* seqlens, int B, int H, int 
   return launch_combine(a, D, out_dtype, static_cast<cudaStream_t>(stream), false);
 }
 
-extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b, int64_t sk_h,
-                              int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
-                              const int32_t* seqlens, int B, int H, int KVH, int S, int D, float scale, int nsplit,
-                              int chunk, int dtype, void* workspace, size_t workspace_bytes, void* out, int64_t so_b,
-                              int64_t so_h, int out_dtype, void* stream) {
+extern "C" int b2d_gqa_decode_ex(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b,
+                                 int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                                 const int32_t* seqlens, int B, int H, int KVH, int S, int D, float scale, int nsplit,
+                                 int chunk, int dtype, void* workspace, size_t workspace_bytes, void* out,
+                                 int64_t so_b, int64_t so_h, int out_dtype, int flags, void* stream) {
   int st = check_attn(B, H, KVH, S, D, dtype);
   if (st != B2D_OK) return st;
   if (out_dtype != dtype && out_dtype != B2D_F32) return B2D_ERR_DTYPE;
@@ -441,8 +492,22 @@ extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const v
   if (nsplit > 65535 || KVH > 65535 || B > 65535) return B2D_ERR_SHAPE;
   a.out = out; a.so_b = so_b; a.so_h = so_h;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((st = launch_partial(a, D, dtype, s)) != B2D_OK) return st;
+  if ((flags & B2D_ATTN_FUSED_COMBINE) && nsplit <= kMaxFusedSplits && B * KVH <= kMaxAttnCounters) {
+    a.fused = 1;
+    a.out_f32 = out_dtype == B2D_F32;
+    return launch_partial(a, D, dtype, s, (flags & B2D_LAUNCH_PDL) != 0);
+  }
+  if ((st = launch_partial(a, D, dtype, s, (flags & B2D_LAUNCH_PDL) != 0)) != B2D_OK) return st;
   return launch_combine(a, D, out_dtype, s, true);
+}
+
+extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b, int64_t sk_h,
+                              int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                              const int32_t* seqlens, int B, int H, int KVH, int S, int D, float scale, int nsplit,
+                              int chunk, int dtype, void* workspace, size_t workspace_bytes, void* out, int64_t so_b,
+                              int64_t so_h, int out_dtype, void* stream) {
+  return b2d_gqa_decode_ex(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
+                           nsplit, chunk, dtype, workspace, workspace_bytes, out, so_b, so_h, out_dtype, 0, stream);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -48,6 +48,13 @@ struct Nf4View {
   const float* code;
 };
 
+constexpr int kMaxSeg = 4;
+struct SegView {
+  Nf4View w;
+  void* y;
+  int64_t ldy;
+};
+
 struct GemmArgs {
   const void* x;
   int64_t ldx;
@@ -60,6 +67,13 @@ struct GemmArgs {
   int total;         // groups * upg
   float* partials;   // [grid][2][E]
   int* counters;     // [groups]
+  // Segmented launches (pipelined kernel only): the row groups of several weights sharing x, in
+  // order. Single-weight launches use one segment equal to (w, y, ldy).
+  int nseg;                  // 1..kMaxSeg
+  int pair;                  // 1: segments 0/1 interleaved per group, epilogue silu(seg0) * seg1
+  int static_w;              // 1: weights may be read before the preceding kernel completes
+  int seg_end[kMaxSeg];      // exclusive end (in row groups) of each segment
+  SegView seg[kMaxSeg];
 };
 
 // One unit of work for one thread, loaded a unit ahead: its weight bytes, the raw per-block scales
@@ -213,6 +227,61 @@ __device__ __forceinline__ void store_group(const GemmArgs& a, int grp, const fl
   }
 }
 
+__device__ __forceinline__ int seg_of(const GemmArgs& a, int grp) {
+  int s = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxSeg - 1; ++i) s += (i + 1 < a.nseg && grp >= a.seg_end[i]) ? 1 : 0;
+  return s;
+}
+
+// SwiGLU in the model dtype, as a Mistral MLP computes it: act_fn(gate_proj(x)) * up_proj(x) with
+// every intermediate rounded to OT.
+template <typename OT>
+__device__ __forceinline__ OT silu_mul(float gate, float up) {
+  const float gq = Dt<OT>::to_f32(Dt<OT>::from_f32(gate));
+  const float sq = Dt<OT>::to_f32(Dt<OT>::from_f32(gq / (1.0f + expf(-gq))));
+  return Dt<OT>::from_f32(sq * Dt<OT>::to_f32(Dt<OT>::from_f32(up)));
+}
+
+// store_group for segmented launches (32-row groups): plain segments write their own output; in
+// paired mode tile 0 holds rows of segment 0 and tile 1 the same rows of segment 1, and the
+// output (segment 0's y) receives silu(tile 0) * tile 1.
+template <typename OT, int NT>
+__device__ __forceinline__ void store_seg(const GemmArgs& a, int grp, const float (&v)[2][NT][4], int g, int tq) {
+  if (a.pair) {
+    OT* y = static_cast<OT*>(a.seg[0].y);
+    const int64_t ldy = a.seg[0].ldy;
+    const int64_t r0 = static_cast<int64_t>(grp) * 16 + g;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int t = nt * 8 + 2 * tq + (c & 1);
+        if (t < a.M) y[t * ldy + r0 + (c >> 1) * 8] = silu_mul<OT>(v[0][nt][c], v[1][nt][c]);
+      }
+    return;
+  }
+  const int s = seg_of(a, grp);
+  OT* y = static_cast<OT*>(a.seg[s].y);
+  const int64_t ldy = a.seg[s].ldy;
+  const int64_t base = static_cast<int64_t>(grp - (s ? a.seg_end[s - 1] : 0)) * 32 + g;
+#pragma unroll
+  for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int t = nt * 8 + 2 * tq + (c & 1);
+        if (t < a.M) y[t * ldy + base + rt * 16 + (c >> 1) * 8] = Dt<OT>::from_f32(v[rt][nt][c]);
+      }
+}
+
+template <typename OT, int RT, int NT, bool SEG>
+__device__ __forceinline__ void store_out(const GemmArgs& a, int grp, const float (&v)[RT][NT][4], int g, int tq) {
+  if constexpr (SEG) store_seg<OT, NT>(a, grp, v, g, tq);
+  else store_group<OT, RT, NT>(a, grp, v, g, tq);
+}
+
 template <int RT, int NT>
 __device__ __forceinline__ void zero_acc(float (&acc)[RT][NT][4]) {
 #pragma unroll
@@ -230,7 +299,7 @@ __device__ __forceinline__ int cta_of(int p, int total, int grid) { return ((p +
 // Combine the per-warp partials of the row groups this CTA touched: warp i handles the i-th group
 // (lanes own their fragment positions); its contributing warps are the contiguous range holding the
 // group's units. Groups shared with neighbouring CTAs go through the workspace (see below).
-template <typename OT, int RT, int NT, int NW>
+template <typename OT, int RT, int NT, int NW, bool SEG>
 __device__ __forceinline__ void combine_cta(const GemmArgs& a, const float* slots, const int* s_wa, const int* s_wb,
                                             const int* s_fg, int A, int B, int cta, int warp, int lane, int g,
                                             int tq) {
@@ -258,7 +327,7 @@ __device__ __forceinline__ void combine_cta(const GemmArgs& a, const float* slot
         }
     }
     if (!shared) {
-      store_group<OT, RT, NT>(a, grp, v, g, tq);
+      store_out<OT, RT, NT, SEG>(a, grp, v, g, tq);
       continue;
     }
     // Shared with neighbouring CTAs: publish this CTA's partial; the last arriver adds all partials
@@ -293,7 +362,7 @@ __device__ __forceinline__ void combine_cta(const GemmArgs& a, const float* slot
           v[rt][nt][0] += q.x; v[rt][nt][1] += q.y; v[rt][nt][2] += q.z; v[rt][nt][3] += q.w;
         }
     }
-    store_group<OT, RT, NT>(a, grp, v, g, tq);
+    store_out<OT, RT, NT, SEG>(a, grp, v, g, tq);
   }
 }
 
@@ -389,7 +458,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
   }
   __syncthreads();
 
-  combine_cta<OT, RT, NT, NW>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
+  combine_cta<OT, RT, NT, NW, false>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -397,64 +466,109 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_tc_kernel(const GemmArgs 
 // streams its units through a private ring of R shared-memory stages filled by 16-byte cp.async
 // copies (8 lanes per 128-byte row segment, so one copy instruction moves 4 whole rows), with the
 // per-row scales riding in the same stage. R-1 units per warp are in flight while one is computed,
-// and no registers hold them. Inside a stage, the 16-byte chunk c of row r sits at chunk
-// c ^ 2*(r & 3): the fragment reads (8 bytes per lane, 4 rows x 2 chunks per half-warp) then hit 32
-// distinct banks without padding.
+// and no registers hold them; the activations of the next unit (all 4 blocks) are loaded into
+// registers while the current one is computed. Inside a stage, the 16-byte chunk c of row r sits at
+// chunk c ^ 2*(r & 3): the fragment reads (8 bytes per lane, 4 rows x 2 chunks per half-warp) then
+// hit 32 distinct banks without padding.
+//
+// The kernel also serves segmented launches: several weights that share x (q/k/v, or gate/up)
+// in one launch, their row groups concatenated. In paired mode a 32-row group is 16 rows of
+// segment 0 (tile 0) and the same 16 rows of segment 1 (tile 1), and the epilogue writes
+// silu(seg0 . x) * (seg1 . x) with the rounding of the model dtype (the SwiGLU of a Mistral MLP).
 constexpr int kStageW = 32 * 128;                // weights of one unit: 32 rows x 4 blocks x 32 B
 constexpr int kStageBytes = kStageW + 32 * 16;   // + scales, 16 B per row
 
 __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (2 * (r & 3))) << 4); }
 
-template <bool NESTED>
-__device__ __forceinline__ void issue_unit(uint32_t st, const GemmArgs& a, int grp, int unit, int lane) {
-  const int64_t row0 = static_cast<int64_t>(grp) * 32;
-  const int c = lane & 7;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3);
-    cp_async16(st + swz(r, c), a.w.packed + (row0 + r) * a.w.ld_packed + unit * 128 + c * 16);
-  }
-  const int64_t row = row0 + lane;
-  const int64_t bi = row * a.w.ld_absmax + static_cast<int64_t>(unit) * 4;
-  if (NESTED) {
-    // a unit never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
-    cp_async4(st + kStageW + lane * 16, static_cast<const uint8_t*>(a.w.absmax) + bi);
-    cp_async4(st + kStageW + lane * 16 + 4,
-              a.w.absmax2 + ((a.w.gblk_base + row * a.w.gblk_row_stride + unit * 4) >> 8));
+// Rows 0..15 and 16..31 of group grp: their segments and the segment-local index of their first row.
+__device__ __forceinline__ void halves_of(const GemmArgs& a, int grp, int& s_lo, int& s_hi, int64_t& r_lo,
+                                          int64_t& r_hi) {
+  if (a.pair) {
+    s_lo = 0; s_hi = 1;
+    r_lo = r_hi = static_cast<int64_t>(grp) * 16;
   } else {
-    cp_async16(st + kStageW + lane * 16, static_cast<const float*>(a.w.absmax) + bi);
+    s_lo = s_hi = seg_of(a, grp);
+    r_lo = static_cast<int64_t>(grp - (s_lo ? a.seg_end[s_lo - 1] : 0)) * 32;
+    r_hi = r_lo + 16;
   }
 }
 
-// One staged unit for a warp: 2 row tiles x 4 blocks. xv holds the activations of the unit's first
-// block on entry and of the next unit's first block on exit (when there is a next unit).
+template <bool NESTED>
+__device__ __forceinline__ void issue_unit(uint32_t st, const GemmArgs& a, int grp, int unit, int lane) {
+  int s_lo, s_hi;
+  int64_t r_lo, r_hi;
+  halves_of(a, grp, s_lo, s_hi, r_lo, r_hi);
+  const int c = lane & 7, rr = lane >> 3;
+  const Nf4View& wl = a.seg[s_lo].w;
+  const Nf4View& wh = a.seg[s_hi].w;
+  const uint8_t* pl = wl.packed + (r_lo + rr) * wl.ld_packed + unit * 128 + c * 16;
+  const uint8_t* ph = wh.packed + (r_hi + rr) * wh.ld_packed + unit * 128 + c * 16;
+  const int64_t sl = 4 * wl.ld_packed, sh = 4 * wh.ld_packed;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cp_async16(st + swz(4 * i + rr, c), pl + i * sl);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cp_async16(st + swz(16 + 4 * i + rr, c), ph + i * sh);
+  const bool hi = lane >= 16;
+  const Nf4View& w = hi ? wh : wl;
+  const int64_t row = (hi ? r_hi : r_lo) + (lane & 15);
+  const int64_t bi = row * w.ld_absmax + static_cast<int64_t>(unit) * 4;
+  if (NESTED) {
+    // a unit never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
+    cp_async4(st + kStageW + lane * 16, static_cast<const uint8_t*>(w.absmax) + bi);
+    cp_async4(st + kStageW + lane * 16 + 4, w.absmax2 + ((w.gblk_base + row * w.gblk_row_stride + unit * 4) >> 8));
+  } else {
+    cp_async16(st + kStageW + lane * 16, static_cast<const float*>(w.absmax) + bi);
+  }
+}
+
+template <typename T, int NT>
+__device__ __forceinline__ void load_x_unit(uint4 (&xv)[4][NT][2], const GemmArgs& a, int unit, int g, int tq) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) load_x<T, NT>(xv[j], a, unit * 4 + j, g, tq);
+}
+
+// One staged unit for a warp: 2 row tiles x 4 blocks, activations of the unit in xv.
+#ifndef B2D_PIPE_XBLOCKS
+#define B2D_PIPE_XBLOCKS 4   // activation blocks held ahead: the whole next unit (4) or one block (1)
+#endif
+constexpr int kXB = B2D_PIPE_XBLOCKS;
+
+// xv holds the unit's activations: all 4 blocks (kXB == 4), or block 0 (kXB == 1; blocks 1..3 are
+// loaded one block ahead here and block 0 of the next unit, next_blk >= 0, at the end).
 template <typename T, int NT, bool NESTED>
-__device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmArgs& a, int unit, bool have_next,
-                                               uint4 (&xv)[NT][2], float (&acc)[2][NT][4], const uint8_t* lut,
-                                               uint32_t lane4, const float* code2_s, int g, int tq) {
+__device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmArgs& a, int grp, int unit,
+                                               int next_blk, uint4 (&xv)[kXB][NT][2], float (&acc)[2][NT][4],
+                                               const uint8_t* lut, uint32_t lane4, const float* code2_s, int g,
+                                               int tq) {
+  const int s0 = a.pair ? 0 : seg_of(a, grp);
   float sc[2][2][4];
 #pragma unroll
-  for (int rt = 0; rt < 2; ++rt)
+  for (int rt = 0; rt < 2; ++rt) {
+    const int s = a.pair ? rt : s0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint8_t* sp = stage + kStageW + (rt * 16 + h * 8 + g) * 16;
       if (NESTED) {
         const uint32_t q4 = *reinterpret_cast<const uint32_t*>(sp);
         const float a2 = *reinterpret_cast<const float*>(sp + 4);
+        const float off = a.seg[s].w.offset;
+        const float* c2 = code2_s + s * 256;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          sc[rt][h][j] = __fadd_rn(__fmul_rn(code2_s[(q4 >> (8 * j)) & 0xFF], a2), a.w.offset);
+        for (int j = 0; j < 4; ++j) sc[rt][h][j] = __fadd_rn(__fmul_rn(c2[(q4 >> (8 * j)) & 0xFF], a2), off);
       } else {
         const float4 v = *reinterpret_cast<const float4*>(sp);
         sc[rt][h][0] = v.x; sc[rt][h][1] = v.y; sc[rt][h][2] = v.z; sc[rt][h][3] = v.w;
       }
     }
-  const int next_blk = (unit + 1) * 4 < (a.K >> 6) ? (unit + 1) * 4 : 0;   // next unit may open a new group
+  }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint4 xn[NT][2];
-    if (j < 3) load_x<T, NT>(xn, a, unit * 4 + j + 1, g, tq);
-    else if (have_next) load_x<T, NT>(xn, a, next_blk, g, tq);
+    if (kXB == 1) {
+      if (j < 3) load_x<T, NT>(xn, a, unit * 4 + j + 1, g, tq);
+      else if (next_blk >= 0) load_x<T, NT>(xn, a, next_blk, g, tq);
+    }
+    const int jx = kXB == 1 ? 0 : j;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
       const int r = rt * 16 + g;
@@ -474,7 +588,7 @@ __device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmA
         const uint32_t a3 = lut_lookup(lut, w1, lane4, sel1);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[nt][0]);
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[jx][nt][0]);
           if (s == 0) Mma<T>::run0(c[nt], a0, a1, a2, a3, xw[0], xw[1]);
           else Mma<T>::run(c[nt], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
         }
@@ -487,16 +601,16 @@ __device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmA
         acc[rt][nt][3] = fmaf(sc[rt][1][j], c[nt][3], acc[rt][nt][3]);
       }
     }
-    if (j < 3 || have_next) {
+    if (kXB == 1 && (j < 3 || next_blk >= 0)) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) { xv[nt][0] = xn[nt][0]; xv[nt][1] = xn[nt][1]; }
+      for (int nt = 0; nt < NT; ++nt) { xv[0][nt][0] = xn[nt][0]; xv[0][nt][1] = xn[nt][1]; }
     }
   }
 }
 
 template <int NW, int R, int NT>
 constexpr size_t pipe_smem_bytes() {
-  return kLutBytes + kCode2Bytes + static_cast<size_t>(NW) * 2 * (2 * NT * 128) * 4 +
+  return kLutBytes + kMaxSeg * kCode2Bytes + static_cast<size_t>(NW) * 2 * (2 * NT * 128) * 4 +
          static_cast<size_t>(NW) * R * kStageBytes;
 }
 
@@ -506,11 +620,12 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
   constexpr int E = RT * NT * 128;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint8_t* lut = smem;
-  float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);
-  float* slots = code2_s + 256;                                       // [NW][2][E]
+  float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);        // [kMaxSeg][256]
+  float* slots = code2_s + kMaxSeg * 256;                             // [NW][2][E]
   uint8_t* rings = reinterpret_cast<uint8_t*>(slots + NW * 2 * E);   // [NW][R][kStageBytes]
   __shared__ int s_wa[NW], s_wb[NW], s_fg[NW];
 
+  pdl_launch_dependents();   // the next kernel in the stream may start its own prologue
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
@@ -523,10 +638,9 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
 
   uint8_t* ring = rings + warp * (R * kStageBytes);
   const uint32_t ring_s = smem_u32(ring);
-  const float my_code = __ldg(a.w.code + (lane & 15));
-  float my_code2 = 0.f;
-  if (NESTED && tid < 256) my_code2 = __ldg(a.w.code2 + tid);
-  // the first R-1 units are in flight while the table is built
+  if (!a.static_w) pdl_wait();   // weights may be the preceding kernel's output
+  const float my_code = __ldg(a.seg[0].w.code + (lane & 15));
+  // the first R-1 units are in flight while the tables are built
   int igrp = first_grp, iun = wa - first_grp * upg;
 #pragma unroll
   for (int s = 0; s < R - 1; ++s) {
@@ -548,15 +662,17 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
     for (int i = 0; i < 32; ++i) entry[(i + lane) & 31] = val;
   }
   if (NESTED)
-    for (int i = tid; i < 256; i += NW * 32) code2_s[i] = i == tid ? my_code2 : __ldg(a.w.code2 + i);
+    for (int i = tid; i < a.nseg * 256; i += NW * 32) code2_s[i] = __ldg(a.seg[i >> 8].w.code2 + (i & 255));
   __syncthreads();
+  pdl_wait();   // x, the workspace and the outputs belong to the stream order from here on
 
   if (wa < wb) {
     float acc[RT][NT][4];
     zero_acc(acc);
     int cgrp = first_grp, cun = wa - first_grp * upg;
-    uint4 xv[NT][2];
-    load_x<T, NT>(xv, a, cun * 4, g, tq);
+    uint4 xv[kXB][NT][2];
+    if (kXB == 4) load_x_unit<T, NT>(reinterpret_cast<uint4 (&)[4][NT][2]>(xv), a, cun, g, tq);
+    else load_x<T, NT>(xv[0], a, cun * 4, g, tq);
     auto park = [&](int grp) {   // a group this warp holds only part of: leave it for the combine
       float* s = slots + (warp * 2 + (grp == first_grp ? 0 : 1)) * E + lane * 4;
 #pragma unroll
@@ -573,24 +689,33 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
         if (++iun == upg) { iun = 0; ++igrp; }
       }
       cp_async_commit();
+      const int next_unit = cun + 1 < upg ? cun + 1 : 0;   // the next unit may open a new group
+      uint4 xn[kXB][NT][2];
+      if (kXB == 4 && p + 1 < wb) load_x_unit<T, NT>(reinterpret_cast<uint4 (&)[4][NT][2]>(xn), a, next_unit, g, tq);
       cp_async_wait<R - 1>();
       __syncwarp();
-      compute_staged<T, NT, NESTED>(ring + ((p - wa) % R) * kStageBytes, a, cun, p + 1 < wb, xv, acc, lut, lane4,
-                                    code2_s, g, tq);
+      compute_staged<T, NT, NESTED>(ring + ((p - wa) % R) * kStageBytes, a, cgrp, cun,
+                                    p + 1 < wb ? next_unit * 4 : -1, xv, acc, lut, lane4, code2_s, g, tq);
       __syncwarp();   // every lane is done with the stage before it is refilled
       if (++cun == upg) {
-        if (cgrp * upg >= wa) store_group<OT, RT, NT>(a, cgrp, acc, g, tq);
+        if (cgrp * upg >= wa) store_seg<OT, NT>(a, cgrp, acc, g, tq);
         else park(cgrp);
         zero_acc(acc);
         cun = 0;
         ++cgrp;
+      }
+      if (kXB == 4 && p + 1 < wb) {
+#pragma unroll
+        for (int j = 0; j < kXB; ++j)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) { xv[j][nt][0] = xn[j][nt][0]; xv[j][nt][1] = xn[j][nt][1]; }
       }
     }
     if (cun != 0) park(cgrp);   // range ended inside a group
   }
   cp_async_wait<0>();
   __syncthreads();
-  combine_cta<OT, RT, NT, NW>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
+  combine_cta<OT, RT, NT, NW, true>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -729,7 +854,7 @@ int launch_tc(const GemmArgs& a, int grid, cudaStream_t stream) {
 #endif
 
 template <typename T, typename OT, bool NESTED, int NW, int R>
-int launch_pipe(const GemmArgs& a, int grid, cudaStream_t stream) {
+int launch_pipe(const GemmArgs& a, int grid, bool pdl, cudaStream_t stream) {
   auto kern = nf4_gemm_pipe_kernel<T, OT, 1, NESTED, NW, R>;
   constexpr size_t smem = pipe_smem_bytes<NW, R, 1>();
   static bool configured[64] = {false};
@@ -740,14 +865,31 @@ int launch_pipe(const GemmArgs& a, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
     configured[dev] = true;
   }
-  kern<<<grid, NW * 32, smem, stream>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
   return launch_status();
+}
+
+template <typename T, typename OT>
+int dispatch_pipe(const GemmArgs& a, int grid, int nested, bool pdl, cudaStream_t s) {
+  return nested ? launch_pipe<T, OT, true, B2D_PIPE_NW, B2D_PIPE_RING>(a, grid, pdl, s)
+                : launch_pipe<T, OT, false, B2D_PIPE_NW, B2D_PIPE_RING>(a, grid, pdl, s);
 }
 
 template <typename T, typename OT, int CB, bool NESTED>
 int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
 #ifndef B2D_PIPE_OFF
-  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, c.grid, s);
+  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, c.grid, false, s);
 #endif
   if (c.nt == 1)
     return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 10>(a, c.grid, s)
@@ -811,7 +953,7 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   if ((st = choose_config(M, N, K, c4, di, &c)) != B2D_OK) return st;
   if (!workspace || workspace_bytes < c.counter_bytes + c.partial_bytes) return B2D_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return B2D_ERR_ALIGN;
-  GemmArgs a;
+  GemmArgs a{};
   a.x = x; a.ldx = ldx;
   a.w = Nf4View{packed, ld_packed, absmax, ld_absmax, code2, absmax2, offset, gblk_base, gblk_row_stride, code};
   a.y = y; a.ldy = ldy;
@@ -821,6 +963,11 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   a.total = static_cast<int>(c.total);
   a.counters = static_cast<int*>(workspace);
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + c.counter_bytes);
+  a.nseg = 1;
+  a.pair = 0;
+  a.static_w = 0;
+  a.seg_end[0] = a.groups;
+  a.seg[0] = SegView{a.w, y, ldy};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == B2D_F16)
     return y_dtype == B2D_F32 ? dispatch_tc<__half, float>(a, c, nested, s) : dispatch_tc<__half, __half>(a, c, nested, s);
@@ -872,4 +1019,68 @@ extern "C" int b2d_nf4_gemv_simt(const void* x, int64_t ldx, const uint8_t* pack
                               : launch_simt_n<__half, __half>(a, grid, nested, s);
   return y_dtype == B2D_F32 ? launch_simt_n<__nv_bfloat16, float>(a, grid, nested, s)
                             : launch_simt_n<__nv_bfloat16, __nv_bfloat16>(a, grid, nested, s);
+}
+
+// ------------------------------------------------------------------------------------------ segmented
+// Several weights on one x in one launch of the pipelined kernel (q/k/v or the paired gate/up of a
+// decoder layer). No counterpart in the reference, which launches one kernel per projection.
+extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
+                                  int M, int K, int dtype, int y_dtype, int mode, int flags, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!segs || nseg < 1 || nseg > kMaxSeg || M < 0 || K < 0) return B2D_ERR_ARG;
+  if (mode != B2D_SEG_INDEPENDENT && mode != B2D_SEG_SILU_MUL) return B2D_ERR_ARG;
+  const bool pair = mode == B2D_SEG_SILU_MUL;
+  if (pair && (nseg != 2 || segs[0].N != segs[1].N || y_dtype != dtype)) return B2D_ERR_SHAPE;
+  int64_t n_total = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const b2d_nf4_segment& sg = segs[i];
+    if (sg.N < 0) return B2D_ERR_ARG;
+    if (sg.N % (pair ? 16 : 32) != 0) return B2D_ERR_SHAPE;
+    // x, y, code and the shared constraints are checked per segment by the single-weight rules
+    int st = check_weight_args(x, ldx, sg.packed, sg.ld_packed, sg.absmax, sg.ld_absmax, nested, sg.code2, sg.absmax2,
+                               segs[0].code, pair && i == 1 ? segs[0].y : sg.y, pair && i == 1 ? segs[0].ldy : sg.ldy,
+                               M, sg.N, K, dtype, y_dtype, 8);
+    if (st != B2D_OK) return st;
+    if (!chunk4_ok(K, sg.absmax, sg.ld_absmax, nested, sg.gblk_base, sg.gblk_row_stride)) return B2D_ERR_ALIGN;
+    n_total += sg.N;
+  }
+  if (M == 0 || n_total == 0) return B2D_OK;
+  DeviceInfo di;
+  int st;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  GemmConfig c;
+  if (n_total > (int64_t(1) << 30)) return B2D_ERR_SHAPE;
+  if ((st = choose_config(M, static_cast<int>(n_total), K, true, di, &c)) != B2D_OK) return st;
+  if (c.nt != 1 || c.rt != 2 || c.cb != 4) return B2D_ERR_SHAPE;
+  if (!workspace || workspace_bytes < c.counter_bytes + c.partial_bytes) return B2D_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return B2D_ERR_ALIGN;
+  GemmArgs a{};
+  a.x = x; a.ldx = ldx;
+  a.M = M; a.N = static_cast<int>(n_total); a.K = K;
+  a.upg = K / 256;
+  a.groups = static_cast<int>(c.groups);
+  a.total = static_cast<int>(c.total);
+  a.counters = static_cast<int*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + c.counter_bytes);
+  a.nseg = nseg;
+  a.pair = pair ? 1 : 0;
+  a.static_w = (flags & B2D_STATIC_WEIGHTS) ? 1 : 0;
+  int end = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const b2d_nf4_segment& sg = segs[i];
+    a.seg[i] = SegView{Nf4View{sg.packed, sg.ld_packed, sg.absmax, sg.ld_absmax, sg.code2, sg.absmax2, sg.offset,
+                               sg.gblk_base, sg.gblk_row_stride, segs[0].code},
+                       sg.y, sg.ldy};
+    end += pair ? sg.N / 16 : sg.N / 32;   // paired: both segments advance together
+    a.seg_end[i] = pair ? sg.N / 16 : end;
+  }
+  a.w = a.seg[0].w;
+  a.y = a.seg[0].y; a.ldy = a.seg[0].ldy;
+  const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B2D_F16)
+    return y_dtype == B2D_F32 ? dispatch_pipe<__half, float>(a, c.grid, nested, pdl, s)
+                              : dispatch_pipe<__half, __half>(a, c.grid, nested, pdl, s);
+  return y_dtype == B2D_F32 ? dispatch_pipe<__nv_bfloat16, float>(a, c.grid, nested, pdl, s)
+                            : dispatch_pipe<__nv_bfloat16, __nv_bfloat16>(a, c.grid, nested, pdl, s);
 }

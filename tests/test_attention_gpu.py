@@ -126,7 +126,7 @@ def test_split_plan_and_workspace():
     assert ns * chunk >= 2048 and chunk % 32 == 0
     assert ns == -(-2048 // chunk)
     lib = _lib.load()
-    assert lib.b2d_gqa_workspace_bytes(8, 32, ns, 128) == 8 * 32 * ns * 130 * 4
+    assert lib.b2d_gqa_workspace_bytes(8, 32, ns, 128) == 65536 + 8 * 32 * ns * 130 * 4
 
 
 def test_rejects_bad_inputs():
@@ -138,3 +138,28 @@ def test_rejects_bad_inputs():
     with pytest.raises(_lib.B2DError):
         decode_attention(torch.randn(1, 32, 1, 96, device=DEV).half(), torch.randn(1, 8, 16, 96, device=DEV).half(),
                          torch.randn(1, 8, 16, 96, device=DEV).half(), 0.1)
+
+
+@pytest.mark.parametrize("B,H,KVH,S,D", [(8, 32, 8, 320, 128), (3, 64, 4, 1000, 64), (2, 32, 8, 4096, 128)])
+@pytest.mark.parametrize("odt", [torch.float16, torch.float32])
+def test_single_launch_combine_matches_two_kernels(B, H, KVH, S, D, odt):
+    """B2D_ATTN_FUSED_COMBINE (the last split CTA combines) gives the two-kernel result bit for bit,
+    including empty and ragged sequences, and leaves the workspace counters at zero."""
+    g = torch.Generator().manual_seed(S + B)
+    q = torch.randn(B, H, 1, D, generator=g).half().to(DEV)
+    k = torch.randn(B, KVH, S, D, generator=g).half().to(DEV)
+    v = torch.randn(B, KVH, S, D, generator=g).half().to(DEV)
+    lens = torch.randint(1, S + 1, (B,), generator=g).to(torch.int32)
+    lens[0] = 0
+    sl = lens.to(DEV)
+    ws = torch.zeros(_lib.load().b2d_gqa_workspace_bytes(B, H, 64, D), dtype=torch.uint8, device=DEV)
+    for chunk in (64, 128, None):
+        two = decode_attention(q, k, v, D ** -0.5, chunk=chunk, seqlens=sl, out_dtype=odt, workspace=ws)
+        one = decode_attention(q, k, v, D ** -0.5, chunk=chunk, seqlens=sl, out_dtype=odt, workspace=ws,
+                               flags=_lib.ATTN_FUSED_COMBINE | _lib.LAUNCH_PDL)
+        again = decode_attention(q, k, v, D ** -0.5, chunk=chunk, seqlens=sl, out_dtype=odt, workspace=ws,
+                                 flags=_lib.ATTN_FUSED_COMBINE)
+        torch.cuda.synchronize()
+        assert torch.equal(one, two) and torch.equal(again, two), chunk
+        assert one[0].abs().max().item() == 0
+    assert ws[:65536].view(torch.int32).abs().sum().item() == 0

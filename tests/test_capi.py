@@ -51,7 +51,7 @@ def test_status_strings_and_version():
 
 def test_workspace_size_arithmetic():
     lib = _lib.load()
-    assert lib.b2d_gqa_workspace_bytes(8, 32, 16, 128) == 8 * 32 * 16 * 130 * 4
+    assert lib.b2d_gqa_workspace_bytes(8, 32, 16, 128) == 65536 + 8 * 32 * 16 * 130 * 4
     assert lib.b2d_gqa_workspace_bytes(0, 32, 16, 128) == 0
 
 
