@@ -151,16 +151,51 @@ def traffic_from_profile():
     return None
 
 
+def _init_ranks(args):
+    """(rank, world, device, TPGroup|None). N > 1 runs one process per GPU under torchrun (NCCL)."""
+    import datetime
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N > 1 with torch.distributed.run")
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    if world == 1:
+        return rank, world, dev, None
+    import torch.distributed as dist
+    from b200kernels.tp import TPGroup
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return rank, world, dev, TPGroup(rank, world)
+
+
+def _max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int, dev):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+
+
 def run_b200(args):
     import torch
     from b200kernels import decode as dec
 
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
+    rank, world, dev, tp = _init_ranks(args)
     B, K, W = args.batch, args.steps, args.warmup
     model = dec.build_random_mistral(seed=args.seed, num_hidden_layers=args.layers)
     max_len = PROMPT + 2 * (K + W) + 16
-    eng = dec.DecodeEngine(model, B, max_len)
+    eng = dec.DecodeEngine(model, B, max_len, tp=tp)
     g = torch.Generator().manual_seed(args.seed + 1)
     prompts = torch.randint(0, model.config.vocab_size, (B, PROMPT), generator=g)
     eng.prefill(prompts.to(dev))
@@ -168,7 +203,7 @@ def run_b200(args):
     clk = ClockSampler(dev.index).start()
     for _ in range(W):
         eng.step()
-    torch.cuda.synchronize(dev)
+    _barrier(world, dev)
 
     # ---- device-resident throughput (clock samples kept only inside this window, padded 50 ms)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -185,14 +220,14 @@ def run_b200(args):
     if profile_region:
         torch.cuda.profiler.stop()
     clk.window = (w0 - 0.05, w1 + 0.05)
-    ms = s.elapsed_time(e)
+    ms = _max_over_ranks(s.elapsed_time(e), world, dev)
     value = B * K / (ms / 1e3)
 
     # ---- end to end through the step API: ids host->device, next ids device->host, every step
     host_in = torch.empty(B, dtype=torch.long).pin_memory()
     host_out = torch.empty(B, dtype=torch.long).pin_memory()
     host_in.copy_(eng.next_ids.cpu())
-    torch.cuda.synchronize(dev)
+    _barrier(world, dev)
     t0 = time.perf_counter()
     se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     se.record()
@@ -204,15 +239,16 @@ def run_b200(args):
         host_in.copy_(host_out)
     ee.record()
     torch.cuda.synchronize(dev)
-    e2e_ms = se.elapsed_time(ee)
+    e2e_ms = _max_over_ranks(se.elapsed_time(ee), world, dev)
     e2e_wall = time.perf_counter() - t0
     e2e = B * K / (e2e_ms / 1e3)
-
     clk.stop()
+    _barrier(world, dev)
 
-    # ---- roofline: the model's gate_proj matmuls (14336x4096 NF4) at batch B, launched back to back
-    # from a CUDA graph on the bench stream and timed with events on that stream (no host gaps);
-    # consecutive launches read different weights, so every launch streams its weights from HBM.
+    # ---- roofline: the model's gate_proj matmuls (this rank's 14336/N x 4096 NF4 shards) at batch B,
+    # launched back to back from a CUDA graph on the bench stream and timed with events on that stream
+    # (no host gaps); consecutive launches read different weights, so every launch streams its
+    # weights from HBM.
     x = torch.randn(B, 4096, generator=torch.Generator().manual_seed(3)).half().to(dev)
     gates = [wd["gate"] for wd in eng.w]
     st = torch.cuda.Stream(dev)
@@ -239,28 +275,46 @@ def run_b200(args):
     peak, peak_kind = measured_peaks()
     achieved = alg / (us * 1e-6) / 1e9
 
-    # ---- reference CPU path on the host
-    cpu_tok_s, threads, sample, _ = cpu_reference(B, 32, samples=1)
+    # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE+KV append, attention partial +
+    # combine, and the NF4 launches (q/k/v + o + gate/up + down paired at B <= 8, else 7 + SiLU*mul);
+    # plus the final add+RMSNorm
+    per_layer = 5 + (4 if eng.pair else 8)
+    launches_per_step = args.layers * per_layer + 1
 
-    launches_per_step = args.layers * (7 + 2)
-    line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
-            "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic (seeded random prompts, random-init N(0, 0.02^2) weights)",
-            "config": {"workload": f"Mistral-7B-shaped NF4 greedy decode, batch {B}, prompt {PROMPT}, "
-                                   f"{args.layers} layers, CUDA-graph step",
-                       "batch": B, "prompt": PROMPT, "layers": args.layers, "parallelism": "single GPU",
-                       "l2": "no flush: 3.9 GB of weights per step exceed the 126 MB L2"},
-            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
-                    "wall_s": round(e2e_wall, 4)},
-            "roofline": {"bound": "hbm", "kernel": "nf4_gemm_tc_kernel (gate_proj 14336x4096, nested)",
-                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(),
-                         "algorithmic_bytes_per_launch": alg, "avg_launch_us": round(us, 3)},
-            "cpu_baseline": {"value": round(cpu_tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": sample},
-            "gpu_launches": launches_per_step * K,
-            "clocks": clk.summary()}
-    print(json.dumps(line), flush=True)
+    cpu = None
+    if world == 1 and rank == 0:   # the reference CPU path on the host, at N=1 only
+        cpu_tok_s, threads, sample, _ = cpu_reference(B, 32, samples=1)
+        cpu = {"value": round(cpu_tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    _barrier(world, dev)
+    if rank == 0:
+        shard = "" if world == 1 else f" (rank-0 shard {gates[0].N}x{gates[0].K})"
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded random prompts, random-init N(0, 0.02^2) weights)",
+                "config": {"workload": f"Mistral-7B-shaped NF4 greedy decode, batch {B}, prompt {PROMPT}, "
+                                       f"{args.layers} layers, CUDA-graph step",
+                           "batch": B, "prompt": PROMPT, "layers": args.layers,
+                           "parallelism": "single GPU" if world == 1 else f"tp{world} (NCCL all-reduce after "
+                                                                          f"o_proj and down_proj)",
+                           "l2": "no flush: 3.9 GB of weights per step exceed the 126 MB L2"},
+                "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
+                        "d2h_bytes_per_step": B * 8, "wall_s": round(e2e_wall, 4)},
+                "roofline": {"bound": "hbm", "kernel": "nf4_gemm_pipe_kernel (gate_proj" + shard + ", nested)",
+                             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4),
+                             "traffic": traffic_from_profile() if world == 1 else None,
+                             "algorithmic_bytes_per_launch": alg, "avg_launch_us": round(us, 3)},
+                "cpu_baseline": cpu,
+                "gpu_launches": launches_per_step * K,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    eng.graph = None   # a graph holding NCCL calls must go before the process group
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+        _barrier(world, dev)
+        dist.destroy_process_group()
 
 
 def _graph_time_us(fns, reps=3):

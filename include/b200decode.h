@@ -134,9 +134,10 @@ enum { B2D_SEG_INDEPENDENT = 0, B2D_SEG_SILU_MUL = 1 };
  * scales (absmax/code2/absmax2/offset) are their own. Every segment's scales must allow 4-block
  * loads: (K/64) % 4 == 0 and ld_absmax % 4 == 0; nested: gblk_base % 4 == 0 and gblk_row_stride % 4 == 0,
  * plain: 16-byte aligned absmax. Workspace: b2d_nf4_gemm_workspace_bytes(M, sum of N_i, K).
- * flags: B2D_LAUNCH_PDL | B2D_STATIC_WEIGHTS. */
+ * flags: B2D_LAUNCH_PDL | B2D_STATIC_WEIGHTS. code_host: NULL, or a HOST copy of the 16 values of
+ * segs[0].code, passed with the launch so the dequant table is built without a device read. */
 int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
-                       int M, int K, int dtype, int y_dtype, int mode, int flags,
+                       int M, int K, int dtype, int y_dtype, int mode, int flags, const float* code_host,
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* CUDA-core variant (fp32 FMAs, warp-shuffle reductions, no tensor cores) of b2d_nf4_gemm for

@@ -51,7 +51,7 @@ SIGNATURES = {
                               _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                               _p, _i64, _i64, _i32, _p]),
     "b2d_nf4_gemm_multi": (_i32, [_p, _i64, C.POINTER(Nf4Segment), _i32, _i32, _i32, _i32, _i32, _i32,
-                                  _i32, _i32, _p, _sz, _p]),
+                                  _i32, _i32, C.POINTER(C.c_float), _p, _sz, _p]),
     "b2d_gqa_decode_ex": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                  _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                                  _p, _i64, _i64, _i32, _i32, _p]),

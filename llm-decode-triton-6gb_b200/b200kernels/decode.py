@@ -28,6 +28,7 @@ from .decode_attention import decode_attention
 from .glue import add_rmsnorm, rope_kv_append, silu_mul
 from .linear4bit import quantize_model_linears
 from .nf4_gemm import NF4Group, NF4Weight
+from .tp import TPGroup, local_heads, shard_layer
 
 # Mistral-7B-v0.3 shape (the checkpoint the reference profiles, profiling/common.py:11)
 MISTRAL_7B = dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
@@ -61,9 +62,14 @@ class DecodeEngine:
     append, attention (partial + combine), o_proj, add+RMSNorm, gate/up in one launch with the SwiGLU
     epilogue, down_proj (batch > 8: separate gate/up launches and a SiLU*mul kernel). ``fused=False``
     keeps the HF modules for the glue ops (the same torch code as the stock path) around the two hot
-    kernels."""
+    kernels.
 
-    def __init__(self, model: MistralForCausalLM, batch: int, max_len: int, fused: bool = True):
+    ``tp`` (a ``TPGroup`` of world size > 1, one process per GPU) runs the tensor-parallel mode: this
+    rank keeps its NF4 shards and its KV heads, and the o_proj / down_proj outputs are all-reduced
+    (NCCL, captured in the step's CUDA graph). Requires ``fused=True``."""
+
+    def __init__(self, model: MistralForCausalLM, batch: int, max_len: int, fused: bool = True,
+                 tp: TPGroup | None = None):
         cfg = model.config
         self.model = model
         self.B, self.S = batch, max_len
@@ -71,14 +77,23 @@ class DecodeEngine:
         self.H, self.KVH = cfg.num_attention_heads, cfg.num_key_value_heads
         self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.H
         self.scale = self.D ** -0.5
+        self.tp = tp if tp is not None and tp.world > 1 else None
+        self.kv0 = 0
+        if self.tp is not None:
+            if not fused:
+                raise ValueError("tensor parallel decode needs fused=True")
+            _, self.H, self.kv0, self.KVH = local_heads(cfg, self.tp.world, self.tp.rank)
         p = next(model.parameters())
         self.device, self.dtype = p.device, model.model.embed_tokens.weight.dtype
         self.w = []
         for layer in model.model.layers:
             at, mlp = layer.self_attn, layer.mlp
-            self.w.append({n: NF4Weight(m.weight) for n, m in (
+            full = {n: NF4Weight(m.weight) for n, m in (
                 ("q", at.q_proj), ("k", at.k_proj), ("v", at.v_proj), ("o", at.o_proj),
-                ("gate", mlp.gate_proj), ("up", mlp.up_proj), ("down", mlp.down_proj))})
+                ("gate", mlp.gate_proj), ("up", mlp.up_proj), ("down", mlp.down_proj))}
+            if self.tp is not None:
+                full = shard_layer(full, cfg, self.tp.world, self.tp.rank)
+            self.w.append(full)
         kv_shape = (self.L, batch, self.KVH, max_len, self.D)
         self.k_cache = torch.zeros(kv_shape, dtype=self.dtype, device=self.device)
         self.v_cache = torch.zeros(kv_shape, dtype=self.dtype, device=self.device)
@@ -95,7 +110,7 @@ class DecodeEngine:
 
     def _init_fused(self, cfg):
         B, dev, dt = self.B, self.device, self.dtype
-        hid, inter = cfg.hidden_size, cfg.intermediate_size
+        hid, inter = cfg.hidden_size, self.w[0]["gate"].N
         self.eps = cfg.rms_norm_eps
         self.pair = B <= NF4Group.MAX_M
         self.groups = []
@@ -147,6 +162,8 @@ class DecodeEngine:
                 g["o"].matmul(a2, [self.o_out], flags=STATIC)
             else:
                 w["o"].matmul(a2, out=self.o_out)
+            if self.tp is not None:
+                self.tp.all_reduce(self.o_out)
             add_rmsnorm(self.r, layer.post_attention_layernorm.weight, self.eps, self.xn, x=self.o_out, flags=PDL)
             if self.pair:
                 g["gateup"].matmul(self.xn, [self.h_mlp], flags=STATIC)
@@ -155,6 +172,8 @@ class DecodeEngine:
                 w["gate"].matmul(self.xn, out=self.g_out); w["up"].matmul(self.xn, out=self.h_mlp)
                 silu_mul(self.g_out, self.h_mlp, out=self.h_mlp, flags=PDL)
                 w["down"].matmul(self.h_mlp, out=self.down_out)
+            if self.tp is not None:
+                self.tp.all_reduce(self.down_out)
             x_in = self.down_out
         add_rmsnorm(self.r, m.norm.weight, self.eps, self.xn, x=x_in, flags=PDL)
         logits = self.model.lm_head(self.xn)                        # [B, vocab]
@@ -230,9 +249,10 @@ class DecodeEngine:
         past = DynamicCache()
         out = self.model(input_ids=prompt_ids.to(self.device), past_key_values=past, use_cache=True,
                          logits_to_keep=1)
+        kv = slice(self.kv0, self.kv0 + self.KVH)   # this rank's KV heads (all of them without TP)
         for i in range(self.L):
-            self.k_cache[i, :, :, :P] = past.layers[i].keys
-            self.v_cache[i, :, :, :P] = past.layers[i].values
+            self.k_cache[i, :, :, :P] = past.layers[i].keys[:, kv]
+            self.v_cache[i, :, :, :P] = past.layers[i].values[:, kv]
         first = out.logits[:, -1].argmax(-1)
         self.ids.copy_(first)
         self.next_ids.copy_(first)

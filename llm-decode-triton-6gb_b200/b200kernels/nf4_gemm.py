@@ -183,6 +183,8 @@ class NF4Group:
         self.K, self.nested = w0.K, w0.nested
         self.Ns = [w.N for w in weights]
         self.n_out = [weights[0].N] if self.mode == _lib.SEG_SILU_MUL else self.Ns
+        import ctypes
+        self._code_host = (ctypes.c_float * 16)(*w0.code.float().cpu().tolist())   # codebook passed by value
         self._segs = (_lib.Nf4Segment * len(weights))()
         for i, w in enumerate(weights):
             sg = self._segs[i]
@@ -210,8 +212,8 @@ class NF4Group:
         ws = gemm_workspace(x.device, nbytes)
         dt = _lib.dtype_code(x.dtype)
         _lib.call("b2d_nf4_gemm_multi", x.data_ptr(), x.stride(0), self._segs, len(self.weights), int(self.nested),
-                  M, self.K, dt, _lib.dtype_code(outs[0].dtype), self.mode, flags, ws.data_ptr(), ws.numel(),
-                  _lib.stream_ptr(x.device))
+                  M, self.K, dt, _lib.dtype_code(outs[0].dtype), self.mode, flags, self._code_host, ws.data_ptr(),
+                  ws.numel(), _lib.stream_ptr(x.device))
         return outs
 
 

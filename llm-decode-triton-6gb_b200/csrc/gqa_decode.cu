@@ -88,12 +88,27 @@ __device__ __forceinline__ void load_tile(KvTile<T, D>& kt, const T* kbase, cons
   }
 }
 
+// Physical 16-byte chunk of logical chunk c (4 floats of O) in a row of the cross-warp staging
+// buffer. Thread t writes logical chunks [t*D/16, (t+1)*D/16); the XOR spreads the 8 threads of a
+// quarter-warp (rows 2q, 2q+1 x t = 0..3) over 8 distinct chunk positions modulo 8, so the 16-byte
+// stores and the merge loop's 4-byte reads are free of bank conflicts.
+template <int D>
+__device__ __forceinline__ int o_chunk(int row, int c) {
+  if (D == 128) {
+    const int t = c >> 3;
+    return (t << 3) | ((c & 7) ^ ((t + 4 * (row & 1)) & 7));
+  } else {
+    const int t = c >> 2;
+    return (t << 2) | ((c & 3) ^ (((t >> 1) + 2 * (row & 1)) & 3));
+  }
+}
+
 template <typename T, int D, bool TWO_HALVES>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const AttnArgs a) {
   constexpr int KSTEPS = D / 16;   // MMA k-steps over the head dim
   constexpr int NTILES = D / 8;    // n8 output tiles of O
   constexpr int ROWS = TWO_HALVES ? 16 : 8;
-  __shared__ float s_o[kAttnWarps][ROWS][D];
+  __shared__ __align__(16) float s_o[kAttnWarps][ROWS][D];   // 16-byte chunks swizzled by o_chunk()
   __shared__ float s_m[kAttnWarps][ROWS], s_l[kAttnWarps][ROWS];
 
   pdl_wait();   // no-op unless launched as a programmatic dependent
@@ -222,10 +237,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
       s_m[warp][row] = m_run[r];
       s_l[warp][row] = l_run[r];
     }
+    // the thread's D/4 columns [D/4*t, D/4*t + D/4) as D/16 float4 chunks: o[n][2r] fill the first
+    // half (n = 0..D/8-1), o[n][2r+1] the second
+    float4* dst = reinterpret_cast<float4*>(&s_o[warp][row][0]);
 #pragma unroll
-    for (int n = 0; n < NTILES; ++n) {
-      s_o[warp][row][(D / 4) * tq + n] = o[n][2 * r];
-      s_o[warp][row][(D / 4) * tq + D / 8 + n] = o[n][2 * r + 1];
+    for (int i = 0; i < D / 16; ++i) {
+      const int n0 = (i % (D / 32)) * 4, c = 2 * r + i / (D / 32);
+      dst[o_chunk<D>(row, (D / 16) * tq + i)] = make_float4(o[n0][c], o[n0 + 1][c], o[n0 + 2][c], o[n0 + 3][c]);
     }
   }
   __syncthreads();
@@ -239,10 +257,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
 #pragma unroll
     for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_m[w][row]);
     float acc = 0.f, l = 0.f;
+    const int phys = o_chunk<D>(row, d >> 2) * 4 + (d & 3);
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) {
       const float e = s_m[w][row] == -INFINITY ? 0.f : exp2f(s_m[w][row] - mx);
-      acc += e * s_o[w][row][d];
+      acc += e * s_o[w][row][phys];
       l += e * s_l[w][row];
     }
     const int64_t slot = slot0 + static_cast<int64_t>(row) * a.nsplit;
@@ -289,7 +308,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
 // One CTA per (b, h), one thread per head-dim element. OT: output dtype.
 template <typename OT, int D>
 __global__ void __launch_bounds__(D) gqa_combine_kernel(const AttnArgs a) {
-  pdl_wait();   // partial results of the previous kernel are visible after this
+  pdl_launch_dependents();   // the next kernel (o_proj) may start its weight prefetch
+  pdl_wait();                // partial results of the previous kernel are visible after this
   const int bh = blockIdx.x;
   const int b = bh / a.H, h = bh - b * a.H;
   const int d = threadIdx.x;
@@ -399,10 +419,14 @@ using namespace b2d;
 extern "C" int b2d_gqa_default_splits(int B, int KVH, int S) {
   DeviceInfo di;
   if (device_info(&di) != B2D_OK || B <= 0 || KVH <= 0 || S <= 0) return 1;
+  // About 1.75 CTAs per SM in one wave: measured best on B200 for B in {1, 8} and S from 320 to
+  // 32768 keys (fewer, longer splits beat more waves of short ones: each CTA has a fixed cost), with
+  // at least 64 keys per split (128 from 2048 keys up).
   const int64_t pairs = static_cast<int64_t>(B) * KVH;
-  const int64_t target = static_cast<int64_t>(di.sm_count) * 8;   // ~4 waves at 2 CTAs/SM
-  int64_t ns = (target + pairs - 1) / pairs;
-  const int64_t max_ns = (S + 63) / 64;                          // keep >= 64 keys per split
+  const int64_t target = static_cast<int64_t>(di.sm_count) * 7 / 4;
+  int64_t ns = target / pairs;
+  const int64_t min_chunk = S >= 2048 ? 128 : 64;
+  const int64_t max_ns = (S + min_chunk - 1) / min_chunk;
   if (ns > max_ns) ns = max_ns;
   if (ns < 1) ns = 1;
   // round chunk up to a multiple of 32 keys and recompute the split count

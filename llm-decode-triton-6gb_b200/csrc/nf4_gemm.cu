@@ -72,6 +72,8 @@ struct GemmArgs {
   int nseg;                  // 1..kMaxSeg
   int pair;                  // 1: segments 0/1 interleaved per group, epilogue silu(seg0) * seg1
   int static_w;              // 1: weights may be read before the preceding kernel completes
+  int code_by_value;         // 1: code_v holds segment 0's 16 codebook values (no device read)
+  float code_v[16];
   int seg_end[kMaxSeg];      // exclusive end (in row groups) of each segment
   SegView seg[kMaxSeg];
 };
@@ -493,31 +495,55 @@ __device__ __forceinline__ void halves_of(const GemmArgs& a, int grp, int& s_lo,
   }
 }
 
+// A lane's copy sources for the units of one group: its weight chunk (16 bytes) of rows rr and
+// 16 + rr (rr = lane / 8; rows 4i further are 4i row strides on), and the scales of row `lane`.
+struct IssueCursor {
+  const uint8_t* pl;
+  const uint8_t* ph;
+  int64_t sl, sh;        // 4-row strides in bytes
+  const uint8_t* sa;     // the row's absmax at unit 0 (bytes)
+  const float* a2;       // absmax2 (double quant)
+  int64_t gb;            // the row's first block in the full tensor (double quant)
+};
+
 template <bool NESTED>
-__device__ __forceinline__ void issue_unit(uint32_t st, const GemmArgs& a, int grp, int unit, int lane) {
+__device__ __forceinline__ IssueCursor cursor_for(const GemmArgs& a, int grp, int lane) {
   int s_lo, s_hi;
   int64_t r_lo, r_hi;
   halves_of(a, grp, s_lo, s_hi, r_lo, r_hi);
   const int c = lane & 7, rr = lane >> 3;
   const Nf4View& wl = a.seg[s_lo].w;
   const Nf4View& wh = a.seg[s_hi].w;
-  const uint8_t* pl = wl.packed + (r_lo + rr) * wl.ld_packed + unit * 128 + c * 16;
-  const uint8_t* ph = wh.packed + (r_hi + rr) * wh.ld_packed + unit * 128 + c * 16;
-  const int64_t sl = 4 * wl.ld_packed, sh = 4 * wh.ld_packed;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) cp_async16(st + swz(4 * i + rr, c), pl + i * sl);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) cp_async16(st + swz(16 + 4 * i + rr, c), ph + i * sh);
+  IssueCursor k;
+  k.pl = wl.packed + (r_lo + rr) * wl.ld_packed + c * 16;
+  k.ph = wh.packed + (r_hi + rr) * wh.ld_packed + c * 16;
+  k.sl = 4 * wl.ld_packed;
+  k.sh = 4 * wh.ld_packed;
   const bool hi = lane >= 16;
   const Nf4View& w = hi ? wh : wl;
   const int64_t row = (hi ? r_hi : r_lo) + (lane & 15);
-  const int64_t bi = row * w.ld_absmax + static_cast<int64_t>(unit) * 4;
+  k.sa = static_cast<const uint8_t*>(w.absmax) + row * w.ld_absmax * (NESTED ? 1 : 4);
+  k.a2 = w.absmax2;
+  k.gb = w.gblk_base + row * w.gblk_row_stride;
+  return k;
+}
+
+// Copy one unit (32 rows x 4 blocks + the rows' scales) into stage st. wdst = this lane's chunk slot
+// for row rr (rows 4i on are 512*i bytes further: the swizzle depends on r & 3 only).
+template <bool NESTED>
+__device__ __forceinline__ void issue_unit(uint32_t st, const IssueCursor& k, int unit, uint32_t wdst, int lane) {
+  const int64_t uo = static_cast<int64_t>(unit) * 128;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cp_async16(st + wdst + 512 * i, k.pl + uo + i * k.sl);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cp_async16(st + wdst + 2048 + 512 * i, k.ph + uo + i * k.sh);
+  const uint32_t sdst = st + kStageW + lane * 16;
   if (NESTED) {
     // a unit never straddles a 256-block group of absmax2 (the host guarantees 4-alignment)
-    cp_async4(st + kStageW + lane * 16, static_cast<const uint8_t*>(w.absmax) + bi);
-    cp_async4(st + kStageW + lane * 16 + 4, w.absmax2 + ((w.gblk_base + row * w.gblk_row_stride + unit * 4) >> 8));
+    cp_async4(sdst, k.sa + unit * 4);
+    cp_async4(sdst + 4, k.a2 + ((k.gb + unit * 4) >> 8));
   } else {
-    cp_async16(st + kStageW + lane * 16, static_cast<const float*>(w.absmax) + bi);
+    cp_async16(sdst, k.sa + unit * 16);
   }
 }
 
@@ -527,54 +553,41 @@ __device__ __forceinline__ void load_x_unit(uint4 (&xv)[4][NT][2], const GemmArg
   for (int j = 0; j < 4; ++j) load_x<T, NT>(xv[j], a, unit * 4 + j, g, tq);
 }
 
-// One staged unit for a warp: 2 row tiles x 4 blocks, activations of the unit in xv.
-#ifndef B2D_PIPE_XBLOCKS
-#define B2D_PIPE_XBLOCKS 4   // activation blocks held ahead: the whole next unit (4) or one block (1)
-#endif
-constexpr int kXB = B2D_PIPE_XBLOCKS;
+// Lane L turns row L's raw double-quantised scales (4 code2 indices + the group's absmax2) into the
+// 4 fp32 block scales, in place in the stage.
+__device__ __forceinline__ void decode_scales(uint8_t* stage, const float* c2, float off, int lane) {
+  uint8_t* sp = stage + kStageW + lane * 16;
+  const uint32_t q4 = *reinterpret_cast<const uint32_t*>(sp);
+  const float a2 = *reinterpret_cast<const float*>(sp + 4);
+  float4 v;
+  v.x = __fadd_rn(__fmul_rn(c2[q4 & 0xFF], a2), off);
+  v.y = __fadd_rn(__fmul_rn(c2[(q4 >> 8) & 0xFF], a2), off);
+  v.z = __fadd_rn(__fmul_rn(c2[(q4 >> 16) & 0xFF], a2), off);
+  v.w = __fadd_rn(__fmul_rn(c2[q4 >> 24], a2), off);
+  *reinterpret_cast<float4*>(sp) = v;
+}
 
-// xv holds the unit's activations: all 4 blocks (kXB == 4), or block 0 (kXB == 1; blocks 1..3 are
-// loaded one block ahead here and block 0 of the next unit, next_blk >= 0, at the end).
-template <typename T, int NT, bool NESTED>
-__device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmArgs& a, int grp, int unit,
-                                               int next_blk, uint4 (&xv)[kXB][NT][2], float (&acc)[2][NT][4],
-                                               const uint8_t* lut, uint32_t lane4, const float* code2_s, int g,
-                                               int tq) {
-  const int s0 = a.pair ? 0 : seg_of(a, grp);
+// One staged unit for a warp: 2 row tiles x 4 blocks; xv = the unit's activations. The lane's
+// fragment bytes of block j, row rt*16 + h*8 + g sit at wb + (rt*16 + h*8)*128 + jx[j] (the stage
+// swizzle: chunk c of row r at c ^ 2(r & 3), and r & 3 == g & 3 for all four rows).
+template <typename T, int NT>
+__device__ __forceinline__ void compute_staged(const uint8_t* stage, const uint8_t* wb, const int (&jx)[4],
+                                               const uint4 (&xv)[4][NT][2], float (&acc)[2][NT][4],
+                                               const uint8_t* lut, uint32_t lane4, int g) {
   float sc[2][2][4];
 #pragma unroll
-  for (int rt = 0; rt < 2; ++rt) {
-    const int s = a.pair ? rt : s0;
+  for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const uint8_t* sp = stage + kStageW + (rt * 16 + h * 8 + g) * 16;
-      if (NESTED) {
-        const uint32_t q4 = *reinterpret_cast<const uint32_t*>(sp);
-        const float a2 = *reinterpret_cast<const float*>(sp + 4);
-        const float off = a.seg[s].w.offset;
-        const float* c2 = code2_s + s * 256;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sc[rt][h][j] = __fadd_rn(__fmul_rn(c2[(q4 >> (8 * j)) & 0xFF], a2), off);
-      } else {
-        const float4 v = *reinterpret_cast<const float4*>(sp);
-        sc[rt][h][0] = v.x; sc[rt][h][1] = v.y; sc[rt][h][2] = v.z; sc[rt][h][3] = v.w;
-      }
+      const float4 v = *reinterpret_cast<const float4*>(stage + kStageW + (rt * 16 + h * 8 + g) * 16);
+      sc[rt][h][0] = v.x; sc[rt][h][1] = v.y; sc[rt][h][2] = v.z; sc[rt][h][3] = v.w;
     }
-  }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    uint4 xn[NT][2];
-    if (kXB == 1) {
-      if (j < 3) load_x<T, NT>(xn, a, unit * 4 + j + 1, g, tq);
-      else if (next_blk >= 0) load_x<T, NT>(xn, a, next_blk, g, tq);
-    }
-    const int jx = kXB == 1 ? 0 : j;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
-      const int r = rt * 16 + g;
-      const int cc = 2 * j + (tq >> 1), off = (tq & 1) * 8;
-      const uint2 wg = *reinterpret_cast<const uint2*>(stage + swz(r, cc) + off);
-      const uint2 wh = *reinterpret_cast<const uint2*>(stage + swz(r + 8, cc) + off);
+      const uint2 wg = *reinterpret_cast<const uint2*>(wb + jx[j] + rt * 2048);
+      const uint2 wh = *reinterpret_cast<const uint2*>(wb + jx[j] + rt * 2048 + 1024);
       float c[NT][4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
@@ -588,7 +601,7 @@ __device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmA
         const uint32_t a3 = lut_lookup(lut, w1, lane4, sel1);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[jx][nt][0]);
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[j][nt][0]);
           if (s == 0) Mma<T>::run0(c[nt], a0, a1, a2, a3, xw[0], xw[1]);
           else Mma<T>::run(c[nt], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
         }
@@ -600,10 +613,6 @@ __device__ __forceinline__ void compute_staged(const uint8_t* stage, const GemmA
         acc[rt][nt][2] = fmaf(sc[rt][1][j], c[nt][2], acc[rt][nt][2]);
         acc[rt][nt][3] = fmaf(sc[rt][1][j], c[nt][3], acc[rt][nt][3]);
       }
-    }
-    if (kXB == 1 && (j < 3 || next_blk >= 0)) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) { xv[0][nt][0] = xn[nt][0]; xv[0][nt][1] = xn[nt][1]; }
     }
   }
 }
@@ -638,14 +647,21 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
 
   uint8_t* ring = rings + warp * (R * kStageBytes);
   const uint32_t ring_s = smem_u32(ring);
+  const uint32_t wdst = swz(lane >> 3, lane & 7);
   if (!a.static_w) pdl_wait();   // weights may be the preceding kernel's output
-  const float my_code = __ldg(a.seg[0].w.code + (lane & 15));
-  // the first R-1 units are in flight while the tables are built
+  const float my_code = a.code_by_value ? a.code_v[lane & 15] : __ldg(a.seg[0].w.code + (lane & 15));
+  // The first R-1 units (and the code2 tables, with group 0) are in flight while the dequant table
+  // is built.
+  if (NESTED)
+    for (int i = tid; i < a.nseg * 256; i += NW * 32) cp_async4(smem_u32(code2_s + i), a.seg[i >> 8].w.code2 + (i & 255));
   int igrp = first_grp, iun = wa - first_grp * upg;
+  IssueCursor cur = cursor_for<NESTED>(a, igrp, lane);
+  int cur_grp = igrp;
 #pragma unroll
   for (int s = 0; s < R - 1; ++s) {
     if (wa + s < wb) {
-      issue_unit<NESTED>(ring_s + s * kStageBytes, a, igrp, iun, lane);
+      if (igrp != cur_grp) { cur = cursor_for<NESTED>(a, igrp, lane); cur_grp = igrp; }
+      issue_unit<NESTED>(ring_s + s * kStageBytes, cur, iun, wdst, lane);
       if (++iun == upg) { iun = 0; ++igrp; }
     }
     cp_async_commit();
@@ -661,8 +677,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
 #pragma unroll
     for (int i = 0; i < 32; ++i) entry[(i + lane) & 31] = val;
   }
-  if (NESTED)
-    for (int i = tid; i < a.nseg * 256; i += NW * 32) code2_s[i] = __ldg(a.seg[i >> 8].w.code2 + (i & 255));
+  if (NESTED) cp_async_wait<R - 2>();   // this thread's code2 copies (group 0) have landed
   __syncthreads();
   pdl_wait();   // x, the workspace and the outputs belong to the stream order from here on
 
@@ -670,9 +685,14 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
     float acc[RT][NT][4];
     zero_acc(acc);
     int cgrp = first_grp, cun = wa - first_grp * upg;
-    uint4 xv[kXB][NT][2];
-    if (kXB == 4) load_x_unit<T, NT>(reinterpret_cast<uint4 (&)[4][NT][2]>(xv), a, cun, g, tq);
-    else load_x<T, NT>(xv[0], a, cun * 4, g, tq);
+    int st_c = 0, st_i = R - 1;   // stages of the unit computed / issued next
+    const uint8_t* wbase0 = ring + g * 128 + 8 * tq;
+    int jx[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) jx[j] = (j ^ (g & 3)) << 5;
+    const int c2_lane_seg = lane >> 4;
+    uint4 xa[4][NT][2], xb[4][NT][2];
+    load_x_unit<T, NT>(xa, a, cun, g, tq);
     auto park = [&](int grp) {   // a group this warp holds only part of: leave it for the combine
       float* s = slots + (warp * 2 + (grp == first_grp ? 0 : 1)) * E + lane * 4;
 #pragma unroll
@@ -682,21 +702,26 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
           *reinterpret_cast<float4*>(s + (rt * NT + nt) * 128) =
               make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]);
     };
-    for (int p = wa; p < wb; ++p) {
-      const int ip = p + R - 1;
-      if (ip < wb) {
-        issue_unit<NESTED>(ring_s + ((ip - wa) % R) * kStageBytes, a, igrp, iun, lane);
+    auto step = [&](const uint4 (&xc)[4][NT][2], uint4 (&xn)[4][NT][2], int p) {
+      if (p + R - 1 < wb) {
+        if (igrp != cur_grp) { cur = cursor_for<NESTED>(a, igrp, lane); cur_grp = igrp; }
+        issue_unit<NESTED>(ring_s + st_i * kStageBytes, cur, iun, wdst, lane);
         if (++iun == upg) { iun = 0; ++igrp; }
       }
+      st_i = st_i + 1 == R ? 0 : st_i + 1;
       cp_async_commit();
-      const int next_unit = cun + 1 < upg ? cun + 1 : 0;   // the next unit may open a new group
-      uint4 xn[kXB][NT][2];
-      if (kXB == 4 && p + 1 < wb) load_x_unit<T, NT>(reinterpret_cast<uint4 (&)[4][NT][2]>(xn), a, next_unit, g, tq);
+      if (p + 1 < wb) load_x_unit<T, NT>(xn, a, cun + 1 < upg ? cun + 1 : 0, g, tq);   // may open a new group
       cp_async_wait<R - 1>();
       __syncwarp();
-      compute_staged<T, NT, NESTED>(ring + ((p - wa) % R) * kStageBytes, a, cgrp, cun,
-                                    p + 1 < wb ? next_unit * 4 : -1, xv, acc, lut, lane4, code2_s, g, tq);
+      uint8_t* stage = ring + st_c * kStageBytes;
+      if (NESTED) {
+        const int s = a.pair ? c2_lane_seg : seg_of(a, cgrp);
+        decode_scales(stage, code2_s + s * 256, a.seg[s].w.offset, lane);
+        __syncwarp();
+      }
+      compute_staged<T, NT>(stage, wbase0 + st_c * kStageBytes, jx, xc, acc, lut, lane4, g);
       __syncwarp();   // every lane is done with the stage before it is refilled
+      st_c = st_c + 1 == R ? 0 : st_c + 1;
       if (++cun == upg) {
         if (cgrp * upg >= wa) store_seg<OT, NT>(a, cgrp, acc, g, tq);
         else park(cgrp);
@@ -704,12 +729,10 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
         cun = 0;
         ++cgrp;
       }
-      if (kXB == 4 && p + 1 < wb) {
-#pragma unroll
-        for (int j = 0; j < kXB; ++j)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) { xv[j][nt][0] = xn[j][nt][0]; xv[j][nt][1] = xn[j][nt][1]; }
-      }
+    };
+    for (int p = wa; p < wb; p += 2) {
+      step(xa, xb, p);
+      if (p + 1 < wb) step(xb, xa, p + 1);
     }
     if (cun != 0) park(cgrp);   // range ended inside a group
   }
@@ -1025,8 +1048,8 @@ extern "C" int b2d_nf4_gemv_simt(const void* x, int64_t ldx, const uint8_t* pack
 // Several weights on one x in one launch of the pipelined kernel (q/k/v or the paired gate/up of a
 // decoder layer). No counterpart in the reference, which launches one kernel per projection.
 extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
-                                  int M, int K, int dtype, int y_dtype, int mode, int flags, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+                                  int M, int K, int dtype, int y_dtype, int mode, int flags, const float* code_host,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
   if (!segs || nseg < 1 || nseg > kMaxSeg || M < 0 || K < 0) return B2D_ERR_ARG;
   if (mode != B2D_SEG_INDEPENDENT && mode != B2D_SEG_SILU_MUL) return B2D_ERR_ARG;
   const bool pair = mode == B2D_SEG_SILU_MUL;
@@ -1065,6 +1088,10 @@ extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segm
   a.nseg = nseg;
   a.pair = pair ? 1 : 0;
   a.static_w = (flags & B2D_STATIC_WEIGHTS) ? 1 : 0;
+  if (code_host) {
+    a.code_by_value = 1;
+    for (int i = 0; i < 16; ++i) a.code_v[i] = code_host[i];
+  }
   int end = 0;
   for (int i = 0; i < nseg; ++i) {
     const b2d_nf4_segment& sg = segs[i];

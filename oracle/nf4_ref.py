@@ -206,6 +206,27 @@ def dequantize(packed, absmax, shape, dtype="fp16", nested=False, code2=None, ab
     return round_to(dequantize_f32(packed, sc, code, shape), dtype)
 
 
+def dequantize_view(packed2d, absmax2d, k_cols, dtype="fp16", nested=False, code2=None, absmax2=None,
+                    offset=0.0, gblk_base=0, gblk_row_stride=None, code=NF4_CODE) -> np.ndarray:
+    """Dequant of a strided view of a larger weight (a tensor-parallel shard), as the C ABI defines
+    it: row r of the view holds ``k_cols`` weights in ``packed2d[r, :k_cols // 2]`` with per-block
+    scales ``absmax2d[r, :k_cols // 64]``; a double-quantised block's group scale is
+    ``absmax2[(gblk_base + r * gblk_row_stride + j) // 256]`` -- the block's index in the FULL tensor,
+    as the reference kernel indexes it (``profiling/kernels/nf4_gemm.py:50-51``)."""
+    packed2d = np.asarray(packed2d, np.uint8)
+    n = packed2d.shape[0]
+    nb = k_cols // BLOCK
+    a = np.asarray(absmax2d)[:, :nb]
+    if nested:
+        gidx = (gblk_base + np.arange(n)[:, None] * gblk_row_stride + np.arange(nb)[None, :]) // BLOCK2
+        prod = (np.asarray(code2, np.float32)[a.astype(np.int64)] * np.asarray(absmax2, np.float32)[gidx])
+        sc = (prod.astype(np.float32) + np.float32(offset)).astype(np.float32)
+    else:
+        sc = a.astype(np.float32)
+    out = dequantize_f32(packed2d[:, : k_cols // 2], sc.reshape(-1), code, (n, k_cols))
+    return round_to(out, dtype)
+
+
 def nf4_matmul_ref(x, w_deq, dtype="fp16") -> np.ndarray:
     """The reference path ``x.float() @ dequant(W).float().T`` (``bench_nf4.py:34,38``),
     evaluated in float64 so the oracle itself adds no accumulation error."""
