@@ -547,10 +547,19 @@ __device__ __forceinline__ void issue_unit(uint32_t st, const IssueCursor& k, in
   }
 }
 
+// Activations of one unit (4 blocks). xrow[nt] is the lane's row of x for token nt*8 + g, clamped to
+// a valid row: lanes past M read real data whose MMA output columns are never stored, so the loads
+// need neither a branch nor zeroing.
 template <typename T, int NT>
-__device__ __forceinline__ void load_x_unit(uint4 (&xv)[4][NT][2], const GemmArgs& a, int unit, int g, int tq) {
+__device__ __forceinline__ void load_x_unit(uint4 (&xv)[4][NT][2], const T* const (&xrow)[NT], int unit) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) load_x<T, NT>(xv[j], a, unit * 4 + j, g, tq);
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const T* p = xrow[nt] + (unit * 4 + j) * 64;
+      xv[j][nt][0] = ldg_u4(p);
+      xv[j][nt][1] = ldg_u4(p + 8);
+    }
 }
 
 // Lane L turns row L's raw double-quantised scales (4 code2 indices + the group's absmax2) into the
@@ -619,8 +628,85 @@ __device__ __forceinline__ void compute_staged(const uint8_t* stage, const uint8
 
 template <int NW, int R, int NT>
 constexpr size_t pipe_smem_bytes() {
-  return kLutBytes + kMaxSeg * kCode2Bytes + static_cast<size_t>(NW) * 2 * (2 * NT * 128) * 4 +
+  return kLutBytes + kMaxSeg * kCode2Bytes + static_cast<size_t>(NW + 1) * 2 * (2 * NT * 128) * 4 +
          static_cast<size_t>(NW) * R * kStageBytes;
+}
+
+// Combine for the cluster partition: a CTA sums its warps' parts of every group it touched; a group
+// held by one CTA is stored at once, a group split between CTAs of the cluster is left in part[] and,
+// after a cluster barrier, the first CTA holding it adds the others' parts (distributed shared
+// memory, in rank order) and stores it. A second barrier keeps every CTA's part[] alive until read.
+template <typename OT, int NT, int NW>
+__device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* slots, float* part, const int* s_wa,
+                                                const int* s_wb, const int* s_fg, int A, int B, int U0, int n,
+                                                int q, int cs, int warp, int lane, int g, int tq) {
+  constexpr int E = 2 * NT * 128;
+  const int upg = a.upg;
+  const int gA = A / upg, gB = B > A ? (B - 1) / upg : gA - 1;
+  const int span = B - A;
+  for (int grp = gA + warp; grp <= gB; grp += NW) {
+    const int lo = max(grp * upg, A), hi = min((grp + 1) * upg, B);
+    const bool shared = grp * upg < A || (grp + 1) * upg > B;
+    const int w_lo = ((lo - A + 1) * NW - 1) / span, w_hi = ((hi - 1 - A + 1) * NW - 1) / span;
+    if (!shared && w_lo == w_hi) continue;   // one warp stored it in full
+    float v[2][NT][4];
+    zero_acc(v);
+    for (int w = w_lo; w <= w_hi; ++w) {
+      if (s_wa[w] >= s_wb[w]) continue;
+      const float* s = slots + (w * 2 + (grp == s_fg[w] ? 0 : 1)) * E + lane * 4;
+#pragma unroll
+      for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 t = *reinterpret_cast<const float4*>(s + (rt * NT + nt) * 128);
+          v[rt][nt][0] += t.x; v[rt][nt][1] += t.y; v[rt][nt][2] += t.z; v[rt][nt][3] += t.w;
+        }
+    }
+    if (!shared) {
+      store_seg<OT, NT>(a, grp, v, g, tq);
+      continue;
+    }
+    float* d = part + (grp == gA ? 0 : 1) * E + lane * 4;
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float4*>(d + (rt * NT + nt) * 128) =
+            make_float4(v[rt][nt][0], v[rt][nt][1], v[rt][nt][2], v[rt][nt][3]);
+  }
+  cluster_sync();
+  // owners: warp 0 takes the CTA's first group, warp 1 its last (when shared and first held here)
+  if (warp < 2 && span > 0) {
+    const int grp = warp == 0 ? gA : gB;
+    const bool shared = grp * upg < A || (grp + 1) * upg > B;
+    const int q_lo = ((grp * upg - U0 + 1) * cs - 1) / n;
+    if (shared && q_lo == q && !(warp == 1 && gB == gA)) {
+      const int q_hi = (((grp + 1) * upg - 1 - U0 + 1) * cs - 1) / n;
+      float v[2][NT][4];
+      const float* mine = part + (grp == gA ? 0 : 1) * E + lane * 4;
+#pragma unroll
+      for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 t = *reinterpret_cast<const float4*>(mine + (rt * NT + nt) * 128);
+          v[rt][nt][0] = t.x; v[rt][nt][1] = t.y; v[rt][nt][2] = t.z; v[rt][nt][3] = t.w;
+        }
+      for (int r = q + 1; r <= q_hi; ++r) {
+        if (r * n / cs == (r + 1) * n / cs) continue;   // a rank without units (fewer units than CTAs)
+        const int r_first = (U0 + r * n / cs) / upg;   // rank r's first group
+        const uint32_t la = smem_u32(part + (grp == r_first ? 0 : 1) * E + lane * 4);
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float4 t = ld_dsmem_f4(la + (rt * NT + nt) * 512, r);
+            v[rt][nt][0] += t.x; v[rt][nt][1] += t.y; v[rt][nt][2] += t.z; v[rt][nt][3] += t.w;
+          }
+      }
+      store_seg<OT, NT>(a, grp, v, g, tq);
+    }
+  }
+  cluster_sync();
 }
 
 template <typename T, typename OT, int NT, bool NESTED, int NW, int R>
@@ -631,15 +717,22 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
   const uint8_t* lut = smem;
   float* code2_s = reinterpret_cast<float*>(smem + kLutBytes);        // [kMaxSeg][256]
   float* slots = code2_s + kMaxSeg * 256;                             // [NW][2][E]
-  uint8_t* rings = reinterpret_cast<uint8_t*>(slots + NW * 2 * E);   // [NW][R][kStageBytes]
+  float* part = slots + NW * 2 * E;                                   // [2][E] cluster-shared groups
+  uint8_t* rings = reinterpret_cast<uint8_t*>(part + 2 * E);         // [NW][R][kStageBytes]
   __shared__ int s_wa[NW], s_wb[NW], s_fg[NW];
 
   pdl_launch_dependents();   // the next kernel in the stream may start its own prologue
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
-  const int grid = gridDim.x, cta = blockIdx.x;
-  const int A = cta_begin(cta, a.total, grid), B = cta_begin(cta + 1, a.total, grid);
+  // Cluster partition: cluster c owns row groups [c*G/ncl, (c+1)*G/ncl) whole; its units (group-major)
+  // are split evenly over its cs CTAs, so K is split only inside a cluster (32-bit math: the host
+  // keeps G*ncl and units*cs below 2^31).
+  const int cs = cluster_size(), q = cluster_rank(), cl = cluster_index(), ncl = cluster_count();
+  const int upg0 = a.upg;
+  const int grp0 = cl * a.groups / ncl, grp1 = (cl + 1) * a.groups / ncl;
+  const int U0 = grp0 * upg0, n_cl = (grp1 - grp0) * upg0;
+  const int A = U0 + q * n_cl / cs, B = U0 + (q + 1) * n_cl / cs;
   const int wa = A + warp * (B - A) / NW, wb = A + (warp + 1) * (B - A) / NW;
   const int upg = a.upg;
   const int first_grp = wa / upg;
@@ -656,13 +749,15 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
     for (int i = tid; i < a.nseg * 256; i += NW * 32) cp_async4(smem_u32(code2_s + i), a.seg[i >> 8].w.code2 + (i & 255));
   int igrp = first_grp, iun = wa - first_grp * upg;
   IssueCursor cur = cursor_for<NESTED>(a, igrp, lane);
-  int cur_grp = igrp;
 #pragma unroll
   for (int s = 0; s < R - 1; ++s) {
     if (wa + s < wb) {
-      if (igrp != cur_grp) { cur = cursor_for<NESTED>(a, igrp, lane); cur_grp = igrp; }
       issue_unit<NESTED>(ring_s + s * kStageBytes, cur, iun, wdst, lane);
-      if (++iun == upg) { iun = 0; ++igrp; }
+      if (++iun == upg) {
+        iun = 0;
+        ++igrp;
+        if (wa + s + 1 < wb) cur = cursor_for<NESTED>(a, igrp, lane);
+      }
     }
     cp_async_commit();
   }
@@ -691,8 +786,14 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
 #pragma unroll
     for (int j = 0; j < 4; ++j) jx[j] = (j ^ (g & 3)) << 5;
     const int c2_lane_seg = lane >> 4;
+    const T* xrow[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tok = nt * 8 + g < a.M ? nt * 8 + g : 0;
+      xrow[nt] = static_cast<const T*>(a.x) + tok * a.ldx + tq * 16;
+    }
     uint4 xa[4][NT][2], xb[4][NT][2];
-    load_x_unit<T, NT>(xa, a, cun, g, tq);
+    load_x_unit<T, NT>(xa, xrow, cun);
     auto park = [&](int grp) {   // a group this warp holds only part of: leave it for the combine
       float* s = slots + (warp * 2 + (grp == first_grp ? 0 : 1)) * E + lane * 4;
 #pragma unroll
@@ -702,21 +803,27 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
           *reinterpret_cast<float4*>(s + (rt * NT + nt) * 128) =
               make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]);
     };
+    // scale-decode table and offset of the group being computed (lane's row segment in paired mode)
+    int dseg = a.pair ? c2_lane_seg : seg_of(a, cgrp);
+    const float* dtab = code2_s + dseg * 256;
+    float doff = a.seg[dseg].w.offset;
     auto step = [&](const uint4 (&xc)[4][NT][2], uint4 (&xn)[4][NT][2], int p) {
       if (p + R - 1 < wb) {
-        if (igrp != cur_grp) { cur = cursor_for<NESTED>(a, igrp, lane); cur_grp = igrp; }
         issue_unit<NESTED>(ring_s + st_i * kStageBytes, cur, iun, wdst, lane);
-        if (++iun == upg) { iun = 0; ++igrp; }
+        if (++iun == upg) {
+          iun = 0;
+          ++igrp;
+          if (p + R < wb) cur = cursor_for<NESTED>(a, igrp, lane);   // the next issue opens this group
+        }
       }
       st_i = st_i + 1 == R ? 0 : st_i + 1;
       cp_async_commit();
-      if (p + 1 < wb) load_x_unit<T, NT>(xn, a, cun + 1 < upg ? cun + 1 : 0, g, tq);   // may open a new group
+      if (p + 1 < wb) load_x_unit<T, NT>(xn, xrow, cun + 1 < upg ? cun + 1 : 0);   // may open a new group
       cp_async_wait<R - 1>();
       __syncwarp();
       uint8_t* stage = ring + st_c * kStageBytes;
       if (NESTED) {
-        const int s = a.pair ? c2_lane_seg : seg_of(a, cgrp);
-        decode_scales(stage, code2_s + s * 256, a.seg[s].w.offset, lane);
+        decode_scales(stage, dtab, doff, lane);
         __syncwarp();
       }
       compute_staged<T, NT>(stage, wbase0 + st_c * kStageBytes, jx, xc, acc, lut, lane4, g);
@@ -728,6 +835,11 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
         zero_acc(acc);
         cun = 0;
         ++cgrp;
+        if (NESTED && !a.pair && p + 1 < wb) {
+          dseg = seg_of(a, cgrp);
+          dtab = code2_s + dseg * 256;
+          doff = a.seg[dseg].w.offset;
+        }
       }
     };
     for (int p = wa; p < wb; p += 2) {
@@ -738,7 +850,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
   }
   cp_async_wait<0>();
   __syncthreads();
-  combine_cta<OT, RT, NT, NW, true>(a, slots, s_wa, s_wb, s_fg, A, B, cta, warp, lane, g, tq);
+  combine_cluster<OT, NT, NW>(a, slots, part, s_wa, s_wb, s_fg, A, B, U0, n_cl, q, cs, warp, lane, g, tq);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -876,43 +988,86 @@ int launch_tc(const GemmArgs& a, int grid, cudaStream_t stream) {
 #define B2D_PIPE_RING 3   // stages per warp
 #endif
 
+// Cluster size for the pipelined kernel: K is split only inside a cluster, whose CTAs own whole row
+// groups, so the choice trades load balance (groups per cluster) against the cluster reduction.
+// Picks the size with the fewest units per CTA on the slowest cluster; ties go to the smaller size.
+struct PipeLaunch {
+  int cs, ncl;
+};
+
 template <typename T, typename OT, bool NESTED, int NW, int R>
-int launch_pipe(const GemmArgs& a, int grid, bool pdl, cudaStream_t stream) {
+int launch_pipe(const GemmArgs& a, bool pdl, cudaStream_t stream) {
   auto kern = nf4_gemm_pipe_kernel<T, OT, 1, NESTED, NW, R>;
   constexpr size_t smem = pipe_smem_bytes<NW, R, 1>();
-  static bool configured[64] = {false};
+  constexpr int kSizes[4] = {1, 2, 4, 8};
+  static int max_clusters[64][4] = {};   // per device and size; 0 = not queried yet, -1 = unavailable
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B2D_ERR_DEVICE;
-  if (!configured[dev]) {
+  if (max_clusters[dev][0] == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
-    configured[dev] = true;
+    DeviceInfo di;
+    if (device_info(&di) != B2D_OK) return B2D_ERR_DEVICE;
+    for (int i = 0; i < 4; ++i) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(kSizes[i] * (di.sm_count / kSizes[i]));
+      cfg.blockDim = dim3(NW * 32);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kSizes[i];
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int m = 0;
+      if (cudaOccupancyMaxActiveClusters(&m, kern, &cfg) != cudaSuccess || m <= 0) {
+        cudaGetLastError();
+        m = i == 0 ? di.sm_count : -1;
+      }
+      max_clusters[dev][i] = m;
+    }
   }
+  PipeLaunch best{1, 0};
+  int64_t best_cost = -1;
+  for (int i = 0; i < 4; ++i) {
+    const int m = max_clusters[dev][i];
+    if (m <= 0) continue;
+    const int ncl = m < a.groups ? m : a.groups;
+    const int64_t per_cluster = (static_cast<int64_t>(a.groups) + ncl - 1) / ncl * a.upg;
+    const int64_t cost = (per_cluster + kSizes[i] - 1) / kSizes[i];   // units on the busiest CTA
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = PipeLaunch{kSizes[i], ncl}; }
+  }
+  if (best.ncl <= 0) return B2D_ERR_DEVICE;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(best.cs * best.ncl);
   cfg.blockDim = dim3(NW * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = best.cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
   return launch_status();
 }
 
 template <typename T, typename OT>
-int dispatch_pipe(const GemmArgs& a, int grid, int nested, bool pdl, cudaStream_t s) {
-  return nested ? launch_pipe<T, OT, true, B2D_PIPE_NW, B2D_PIPE_RING>(a, grid, pdl, s)
-                : launch_pipe<T, OT, false, B2D_PIPE_NW, B2D_PIPE_RING>(a, grid, pdl, s);
+int dispatch_pipe(const GemmArgs& a, int nested, bool pdl, cudaStream_t s) {
+  return nested ? launch_pipe<T, OT, true, B2D_PIPE_NW, B2D_PIPE_RING>(a, pdl, s)
+                : launch_pipe<T, OT, false, B2D_PIPE_NW, B2D_PIPE_RING>(a, pdl, s);
 }
 
 template <typename T, typename OT, int CB, bool NESTED>
 int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
 #ifndef B2D_PIPE_OFF
-  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, c.grid, false, s);
+  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, false, s);
 #endif
   if (c.nt == 1)
     return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 10>(a, c.grid, s)
@@ -1106,8 +1261,8 @@ extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segm
   const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == B2D_F16)
-    return y_dtype == B2D_F32 ? dispatch_pipe<__half, float>(a, c.grid, nested, pdl, s)
-                              : dispatch_pipe<__half, __half>(a, c.grid, nested, pdl, s);
-  return y_dtype == B2D_F32 ? dispatch_pipe<__nv_bfloat16, float>(a, c.grid, nested, pdl, s)
-                            : dispatch_pipe<__nv_bfloat16, __nv_bfloat16>(a, c.grid, nested, pdl, s);
+    return y_dtype == B2D_F32 ? dispatch_pipe<__half, float>(a, nested, pdl, s)
+                              : dispatch_pipe<__half, __half>(a, nested, pdl, s);
+  return y_dtype == B2D_F32 ? dispatch_pipe<__nv_bfloat16, float>(a, nested, pdl, s)
+                            : dispatch_pipe<__nv_bfloat16, __nv_bfloat16>(a, nested, pdl, s);
 }
