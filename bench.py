@@ -295,8 +295,8 @@ def run_b200(args):
                 "config": {"workload": f"Mistral-7B-shaped NF4 greedy decode, batch {B}, prompt {PROMPT}, "
                                        f"{args.layers} layers, CUDA-graph step",
                            "batch": B, "prompt": PROMPT, "layers": args.layers,
-                           "parallelism": "single GPU" if world == 1 else f"tp{world} (NCCL all-reduce after "
-                                                                          f"o_proj and down_proj)",
+                           "parallelism": "single GPU" if world == 1 else
+                           f"tp{world} (one-shot NVLink peer-memory all-reduce after o_proj and down_proj)",
                            "l2": "no flush: 3.9 GB of weights per step exceed the 126 MB L2"},
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
                         "d2h_bytes_per_step": B * 8, "wall_s": round(e2e_wall, 4)},
@@ -309,6 +309,8 @@ def run_b200(args):
                 "gpu_launches": launches_per_step * K,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
+    if tp is not None and tp.peer_errors():
+        raise SystemExit(f"rank {rank}: {tp.peer_errors()} timed-out all-reduce waits; the run is invalid")
     eng.graph = None   # a graph holding NCCL calls must go before the process group
     torch.cuda.synchronize(dev)
     if world > 1:

@@ -248,6 +248,21 @@ int b2d_rope_kv_append(const void* q, int64_t ldq, const void* k, int64_t ldk, c
 int b2d_silu_mul(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo,
                  int M, int N, int dtype, int flags, void* stream);
 
+/* ================================================================ tensor-parallel all-reduce
+ * One-shot sum of n elements across `world` GPUs over NVLink peer memory (no counterpart in the
+ * reference, which is single-GPU; used in place of the NCCL all-reduce after o_proj and down_proj).
+ * Every rank owns a buffer of b2d_allreduce_buffer_bytes(n_max, world, dtype) bytes, zero-filled once
+ * before first use and mapped by all peers; peer_bufs is a HOST array of the world buffers' device
+ * addresses as seen from this GPU (peer_bufs[rank] = this rank's own). All ranks must make the same
+ * sequence of calls (same n). out = sum over ranks of in, in rank order in fp32, rounded once: every
+ * rank gets identical bits. in may equal out. n % 8 == 0, n <= n_max, n <= 64 * 4096; dtype F16 or
+ * BF16; world <= 8. A wait that times out (a peer that never arrives) counts one error in the int32
+ * at byte offset 256 of this rank's buffer and the kernel returns (its output is then invalid).
+ * flags: B2D_LAUNCH_PDL. */
+size_t b2d_allreduce_buffer_bytes(int64_t n_max, int world, int dtype);
+int b2d_allreduce(const void* in, void* out, int64_t n, int dtype, void* const* peer_bufs, int rank,
+                  int world, int64_t n_max, int flags, void* stream);
+
 /* b2d_gqa_decode without a caller workspace (no counterpart in the reference). For callers that
  * cannot allocate device memory themselves -- a serving process whose allocator owns the whole device
  * budget, or a plugin inside another framework's memory pool that must not cudaMalloc behind its

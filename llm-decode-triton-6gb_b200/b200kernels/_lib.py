@@ -60,6 +60,8 @@ SIGNATURES = {
                                   _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p,
                                   _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
     "b2d_silu_mul": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _p]),
+    "b2d_allreduce_buffer_bytes": (_sz, [_i64, _i32, _i32]),
+    "b2d_allreduce": (_i32, [_p, _p, _i64, _i32, C.POINTER(C.c_void_p), _i32, _i32, _i64, _i32, _p]),
     "b2d_gqa_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                       _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32,
                                       _p, _i64, _i64, _i32, _p]),

@@ -66,10 +66,11 @@ class DecodeEngine:
 
     ``tp`` (a ``TPGroup`` of world size > 1, one process per GPU) runs the tensor-parallel mode: this
     rank keeps its NF4 shards and its KV heads, and the o_proj / down_proj outputs are all-reduced
-    (NCCL, captured in the step's CUDA graph). Requires ``fused=True``."""
+    inside the step's CUDA graph -- ``allreduce="peer"``: the one-shot NVLink peer-memory kernel
+    (``b2d_allreduce``), ``"nccl"``: NCCL. Requires ``fused=True``."""
 
     def __init__(self, model: MistralForCausalLM, batch: int, max_len: int, fused: bool = True,
-                 tp: TPGroup | None = None):
+                 tp: TPGroup | None = None, allreduce: str = "peer"):
         cfg = model.config
         self.model = model
         self.B, self.S = batch, max_len
@@ -107,6 +108,10 @@ class DecodeEngine:
         self.fused = fused
         if fused:
             self._init_fused(cfg)
+        if self.tp is not None and allreduce == "peer":
+            self.tp.enable_peer_allreduce(batch * cfg.hidden_size, self.dtype, self.device)
+        elif self.tp is not None and allreduce != "nccl":
+            raise ValueError(f"allreduce must be 'peer' or 'nccl', got {allreduce!r}")
 
     def _init_fused(self, cfg):
         B, dev, dt = self.B, self.device, self.dtype

@@ -27,15 +27,52 @@ ROWWISE = ("o", "down")
 @dataclass
 class TPGroup:
     """This process's place in the tensor-parallel group (``group`` is a torch.distributed group or
-    None for the default one)."""
+    None for the default one).
+
+    ``all_reduce`` sums a tensor over the group in place: with ``enable_peer_allreduce`` (called once,
+    collectively) through ``b2d_allreduce`` -- every rank pushes its slice into its peers' memory over
+    NVLink and sums locally, one launch -- otherwise through NCCL."""
     rank: int
     world: int
     group: object = None
+    _peer: object = None
+
+    def enable_peer_allreduce(self, n_max: int, dtype, device) -> None:
+        """Map one symmetric buffer per rank (torch symmetric memory: every peer's buffer addressable
+        from this GPU) for the one-shot all-reduce of up to ``n_max`` elements."""
+        import ctypes
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _lib
+        nbytes = _lib.load().b2d_allreduce_buffer_bytes(n_max, self.world, _lib.dtype_code(dtype))
+        if nbytes == 0:
+            raise ValueError(f"unsupported all-reduce size {n_max} / world {self.world} / {dtype}")
+        buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        buf.zero_()
+        torch.cuda.synchronize(device)
+        group = self.group if self.group is not None else dist.group.WORLD
+        hdl = symm_mem.rendezvous(buf, group.group_name)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        dist.barrier(group=group, device_ids=[torch.device(device).index])
+        self._peer = dict(buf=buf, hdl=hdl, n_max=int(n_max), ptrs=(ctypes.c_void_p * self.world)(*ptrs))
+
+    def peer_errors(self) -> int:
+        """Timed-out waits recorded by the peer all-reduce on this rank (0 when healthy)."""
+        if self._peer is None:
+            return 0
+        return int(self._peer["buf"][256:260].view(torch.int32).item())
 
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        if self._peer is not None and t.is_contiguous() and t.numel() <= self._peer["n_max"]:
+            from . import _lib
+            _lib.call("b2d_allreduce", t.data_ptr(), t.data_ptr(), t.numel(), _lib.dtype_code(t.dtype),
+                      self._peer["ptrs"], self.rank, self.world, self._peer["n_max"], _lib.LAUNCH_PDL,
+                      _lib.stream_ptr(t.device))
+            return t
         import torch.distributed as dist
-        if self.world > 1:
-            dist.all_reduce(t, group=self.group)
+        dist.all_reduce(t, group=self.group)
         return t
 
 

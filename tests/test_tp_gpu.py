@@ -28,7 +28,13 @@ def test_tp2_decode_matches_single_gpu():
     res = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     line = [ln for ln in res.stdout.splitlines() if ln.startswith("TP_RESULT")]
     assert res.returncode == 0 and line, res.stdout[-2000:] + res.stderr[-4000:]
-    for r in json.loads(line[0].split(" ", 1)[1]):
-        assert r["max_rel_logit_diff_vs_1gpu"] < 2e-2, r
-        assert r["argmax_agree_vs_1gpu"] >= 0.9, r
-        assert r["greedy_equal_stock"], r
+    ranks = json.loads(line[0].split(" ", 1)[1])
+    for r in ranks:
+        for mode in ("peer", "nccl"):
+            m = r[mode]
+            assert m["max_rel_logit_diff_vs_1gpu"] < 2e-2, (mode, r)
+            assert m["argmax_agree_vs_1gpu"] >= 0.9, (mode, r)
+            assert m["greedy_equal_stock"], (mode, r)
+            assert m["peer_errors"] == 0, (mode, r)
+    # the peer all-reduce gives every rank identical sums, so identical logits
+    assert len({r["peer"]["logits_sum"] for r in ranks}) == 1, ranks

@@ -30,16 +30,21 @@ def main():
         B = 4
         ids = torch.randint(0, SMALL["vocab_size"], (B, 32), generator=torch.Generator().manual_seed(5)).to(dev)
         stock = dec.hf_greedy(model, ids, 12)
-        tp_eng = dec.DecodeEngine(model, B, 64, tp=TPGroup(rank, world))
-        p_tp, l_tp = tp_eng.teacher_forced(ids, stock)
-        ours = tp_eng.generate(ids, 12)
-        tp_eng.graph = None
         one = dec.DecodeEngine(model, B, 64)
         p_one, l_one = one.teacher_forced(ids, stock)
-        err = (l_tp - l_one).abs().max().item() / l_one.abs().max().item()
-        res = {"rank": rank, "world": world, "max_rel_logit_diff_vs_1gpu": err,
-               "argmax_agree_vs_1gpu": (p_tp == p_one).float().mean().item(),
-               "greedy_equal_stock": bool(torch.equal(ours, stock))}
+        res = {"rank": rank, "world": world}
+        for mode in ("peer", "nccl"):
+            grp = TPGroup(rank, world)
+            tp_eng = dec.DecodeEngine(model, B, 64, tp=grp, allreduce=mode)
+            p_tp, l_tp = tp_eng.teacher_forced(ids, stock)
+            ours = tp_eng.generate(ids, 12)
+            tp_eng.graph = None
+            torch.cuda.synchronize(dev)
+            res[mode] = {"max_rel_logit_diff_vs_1gpu": (l_tp - l_one).abs().max().item() / l_one.abs().max().item(),
+                         "argmax_agree_vs_1gpu": (p_tp == p_one).float().mean().item(),
+                         "greedy_equal_stock": bool(torch.equal(ours, stock)), "peer_errors": grp.peer_errors(),
+                         "logits_sum": float(l_tp.double().sum())}
+            dist.barrier(device_ids=[dev.index])
         out = [None] * world
         dist.all_gather_object(out, res)
         if rank == 0:
