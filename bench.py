@@ -194,11 +194,15 @@ def run_b200(args):
     rank, world, dev, tp = _init_ranks(args)
     B, K, W = args.batch, args.steps, args.warmup
     model = dec.build_random_mistral(seed=args.seed, num_hidden_layers=args.layers)
-    max_len = PROMPT + 2 * (K + W) + 16
+    context = args.context or PROMPT
+    max_len = context + 2 * (K + W) + 16
     eng = dec.DecodeEngine(model, B, max_len, tp=tp)
-    g = torch.Generator().manual_seed(args.seed + 1)
-    prompts = torch.randint(0, model.config.vocab_size, (B, PROMPT), generator=g)
-    eng.prefill(prompts.to(dev))
+    if args.context:   # long caches: seeded K/V written straight into the static cache (no prefill)
+        eng.fill_random_cache(context, seed=args.seed + 1)
+    else:
+        g = torch.Generator().manual_seed(args.seed + 1)
+        prompts = torch.randint(0, model.config.vocab_size, (B, PROMPT), generator=g)
+        eng.prefill(prompts.to(dev))
     eng.capture()
     clk = ClockSampler(dev.index).start()
     for _ in range(W):
@@ -275,10 +279,12 @@ def run_b200(args):
     peak, peak_kind = measured_peaks()
     achieved = alg / (us * 1e-6) / 1e9
 
-    # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE+KV append, attention partial +
-    # combine, and the NF4 launches (q/k/v + o + gate/up + down paired at B <= 8, else 7 + SiLU*mul);
-    # plus the final add+RMSNorm
-    per_layer = 5 + (4 if eng.pair else 8)
+    # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE + KV append, attention partial +
+    # combine and the NF4 launches (q/k/v, o, gate/up, down at B <= 8; else 7 NF4 launches and SiLU*mul),
+    # plus the all-reduces under TP; plus the final add+RMSNorm
+    per_layer = (5 + 4) if eng.pair else (5 + 7 + 1)
+    if tp is not None:
+        per_layer += 2
     launches_per_step = args.layers * per_layer + 1
 
     cpu = None
@@ -292,9 +298,11 @@ def run_b200(args):
                 "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded random prompts, random-init N(0, 0.02^2) weights)",
-                "config": {"workload": f"Mistral-7B-shaped NF4 greedy decode, batch {B}, prompt {PROMPT}, "
-                                       f"{args.layers} layers, CUDA-graph step",
-                           "batch": B, "prompt": PROMPT, "layers": args.layers,
+                "config": {"workload": f"Mistral-7B-shaped NF4 greedy decode, batch {B}, "
+                                       + (f"{context}-token seeded random KV cache" if args.context else
+                                          f"prompt {PROMPT}") + f", {args.layers} layers, CUDA-graph step",
+                           "batch": B, "prompt": None if args.context else PROMPT, "context": context,
+                           "layers": args.layers,
                            "parallelism": "single GPU" if world == 1 else
                            f"tp{world} (one-shot NVLink peer-memory all-reduce after o_proj and down_proj)",
                            "l2": "no flush: 3.9 GB of weights per step exceed the 126 MB L2"},
@@ -425,6 +433,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--context", type=int, default=0,
+                    help="decode after a seeded random KV cache of this many tokens instead of a 256-token prefill "
+                         "(long-context and tensor-parallel configurations)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     args = ap.parse_args()
