@@ -196,7 +196,7 @@ def run_b200(args):
     model = dec.build_random_mistral(seed=args.seed, num_hidden_layers=args.layers)
     context = args.context or PROMPT
     max_len = context + 2 * (K + W) + 16
-    eng = dec.DecodeEngine(model, B, max_len, tp=tp)
+    eng = dec.DecodeEngine(model, B, max_len, tp=tp, allreduce=args.allreduce)
     if args.context:   # long caches: seeded K/V written straight into the static cache (no prefill)
         eng.fill_random_cache(context, seed=args.seed + 1)
     else:
@@ -283,7 +283,7 @@ def run_b200(args):
     # combine and the NF4 launches (q/k/v, o, gate/up, down at B <= 8; else 7 NF4 launches and SiLU*mul),
     # plus the all-reduces under TP; plus the final add+RMSNorm
     per_layer = (5 + 4) if eng.pair else (5 + 7 + 1)
-    if tp is not None:
+    if tp is not None and not eng.ar_fused:   # fused: the GEMMs push, the add+RMSNorm launches sum
         per_layer += 2
     launches_per_step = args.layers * per_layer + 1
 
@@ -304,7 +304,12 @@ def run_b200(args):
                            "batch": B, "prompt": None if args.context else PROMPT, "context": context,
                            "layers": args.layers,
                            "parallelism": "single GPU" if world == 1 else
-                           f"tp{world} (one-shot NVLink peer-memory all-reduce after o_proj and down_proj)",
+                           f"tp{world} (" + {"fused": "o_proj/down_proj GEMM epilogues push partials to the peers "
+                                                     "over NVLink, summed in the next add+RMSNorm",
+                                             "peer": "one-shot NVLink peer-memory all-reduce after o_proj and "
+                                                     "down_proj",
+                                             "nccl": "NCCL all-reduce after o_proj and down_proj"}[
+                               "fused" if eng.ar_fused else ("nccl" if args.allreduce == "nccl" else "peer")] + ")",
                            "l2": "no flush: 3.9 GB of weights per step exceed the 126 MB L2"},
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
                         "d2h_bytes_per_step": B * 8, "wall_s": round(e2e_wall, 4)},
@@ -437,6 +442,8 @@ def main():
                     help="decode after a seeded random KV cache of this many tokens instead of a 256-token prefill "
                          "(long-context and tensor-parallel configurations)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--allreduce", choices=["fused", "peer", "nccl"], default="fused",
+                    help="tensor-parallel all-reduce: fused into the o/down GEMM epilogue, peer-memory kernel, NCCL")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     args = ap.parse_args()
     if args.kernel:

@@ -122,7 +122,22 @@ typedef struct {
   int64_t ldy;
 } b2d_nf4_segment;
 
-enum { B2D_SEG_INDEPENDENT = 0, B2D_SEG_SILU_MUL = 1 };
+enum { B2D_SEG_INDEPENDENT = 0, B2D_SEG_SILU_MUL = 1, B2D_SEG_ALLREDUCE = 2 };
+
+/* Where a tensor-parallel all-reduce fused into a GEMM epilogue sends its partial sums (no counterpart
+ * in the reference, which is single-GPU). Buffers as for b2d_allreduce (one per rank, sized by
+ * b2d_allreduce_buffer_bytes(n_max, world, dtype), zero-filled once, mapped by every peer; a separate
+ * buffer from the one b2d_allreduce uses). The call's epoch is read on the device:
+ * step[0] * sites + site + 1, so a captured CUDA graph stays valid while the caller advances
+ * *step once per decode step (every rank the same way) and gives each all-reduce of a step its own
+ * site in [0, sites). Epochs must keep increasing over the buffer's life. */
+typedef struct {
+  void* const* peer_bufs;   /* HOST array [world]: every rank's buffer as seen from this GPU */
+  int rank, world;          /* world <= 8 */
+  int64_t n_max;            /* elements the buffers were sized for (multiple of 8) */
+  const int64_t* step;      /* device counter */
+  int site, sites;
+} b2d_allreduce_epilogue;
 
 /* Several NF4 weights applied to the same x in ONE launch (no counterpart in the reference, which
  * launches one kernel per projection; this fuses q/k/v and gate/up of a decoder layer).
@@ -134,11 +149,17 @@ enum { B2D_SEG_INDEPENDENT = 0, B2D_SEG_SILU_MUL = 1 };
  * scales (absmax/code2/absmax2/offset) are their own. Every segment's scales must allow 4-block
  * loads: (K/64) % 4 == 0 and ld_absmax % 4 == 0; nested: gblk_base % 4 == 0 and gblk_row_stride % 4 == 0,
  * plain: 16-byte aligned absmax. Workspace: b2d_nf4_gemm_workspace_bytes(M, sum of N_i, K).
+ *   mode B2D_SEG_ALLREDUCE:   nseg == 1, y_dtype == dtype, epilogue = a b2d_allreduce_epilogue: the
+ *                             partial product x @ W_0^T (this rank's K slice of a row-parallel
+ *                             linear, rounded to dtype) is not stored to segs[0].y but written into
+ *                             every peer's buffer, to be summed by b2d_allreduce_add_rmsnorm with the
+ *                             same epilogue descriptor. (M + 1) / 2 * N_0 <= n_max / 2.
  * flags: B2D_LAUNCH_PDL | B2D_STATIC_WEIGHTS. code_host: NULL, or a HOST copy of the 16 values of
- * segs[0].code, passed with the launch so the dequant table is built without a device read. */
+ * segs[0].code, passed with the launch so the dequant table is built without a device read.
+ * epilogue: NULL unless mode is B2D_SEG_ALLREDUCE. */
 int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
                        int M, int K, int dtype, int y_dtype, int mode, int flags, const float* code_host,
-                       void* workspace, size_t workspace_bytes, void* stream);
+                       const void* epilogue, void* workspace, size_t workspace_bytes, void* stream);
 
 /* CUDA-core variant (fp32 FMAs, warp-shuffle reductions, no tensor cores) of b2d_nf4_gemm for
  * 1 <= M <= 8: same arguments and constraints, no workspace. Kept as the measured comparison
@@ -262,6 +283,16 @@ int b2d_silu_mul(const void* gate, int64_t ldg, const void* up, int64_t ldu, voi
 size_t b2d_allreduce_buffer_bytes(int64_t n_max, int world, int dtype);
 int b2d_allreduce(const void* in, void* out, int64_t n, int dtype, void* const* peer_bufs, int rank,
                   int world, int64_t n_max, int flags, void* stream);
+
+/* The consumer half of an all-reduce fused into a GEMM epilogue (B2D_SEG_ALLREDUCE), merged with the
+ * residual add + RMSNorm that follows o_proj / down_proj:
+ *   x = sum over ranks (rank order, fp32, one rounding) of the partials of the epilogue's site;
+ *   residual += x; out = rmsnorm(residual) * weight   -- exactly b2d_allreduce then b2d_add_rmsnorm.
+ * M rows of D (= the GEMM's N; D % 8 == 0, D <= 8192, (M + 1) / 2 * D <= n_max / 2). Waits are
+ * bounded: a peer that never writes counts one error in the int32 at byte offset 256 of this rank's
+ * buffer and the kernel returns. flags: B2D_LAUNCH_PDL. */
+int b2d_allreduce_add_rmsnorm(const b2d_allreduce_epilogue* ar, void* residual, int64_t ldr, const void* weight,
+                              float eps, void* out, int64_t ldo, int M, int D, int dtype, int flags, void* stream);
 
 /* b2d_gqa_decode without a caller workspace (no counterpart in the reference). For callers that
  * cannot allocate device memory themselves -- a serving process whose allocator owns the whole device

@@ -17,7 +17,7 @@ F16, BF16, F32 = 0, 1, 2
 _p, _i64, _i32, _f32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 
 LAUNCH_PDL, STATIC_WEIGHTS, ATTN_FUSED_COMBINE = 1, 2, 4   # launch flags
-SEG_INDEPENDENT, SEG_SILU_MUL = 0, 1         # b2d_nf4_gemm_multi modes
+SEG_INDEPENDENT, SEG_SILU_MUL, SEG_ALLREDUCE = 0, 1, 2   # b2d_nf4_gemm_multi modes
 
 
 class Nf4Segment(C.Structure):
@@ -25,6 +25,12 @@ class Nf4Segment(C.Structure):
     _fields_ = [("packed", _p), ("ld_packed", _i64), ("absmax", _p), ("ld_absmax", _i64),
                 ("code2", _p), ("absmax2", _p), ("offset", _f32), ("gblk_base", _i64),
                 ("gblk_row_stride", _i64), ("code", _p), ("N", _i32), ("y", _p), ("ldy", _i64)]
+
+
+class AllreduceEpilogue(C.Structure):
+    """b2d_allreduce_epilogue (include/b200decode.h)."""
+    _fields_ = [("peer_bufs", C.POINTER(C.c_void_p)), ("rank", _i32), ("world", _i32), ("n_max", _i64),
+                ("step", _p), ("site", _i32), ("sites", _i32)]
 
 
 # name -> (restype, argtypes); mirrors include/b200decode.h
@@ -51,7 +57,7 @@ SIGNATURES = {
                               _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                               _p, _i64, _i64, _i32, _p]),
     "b2d_nf4_gemm_multi": (_i32, [_p, _i64, C.POINTER(Nf4Segment), _i32, _i32, _i32, _i32, _i32, _i32,
-                                  _i32, _i32, C.POINTER(C.c_float), _p, _sz, _p]),
+                                  _i32, _i32, C.POINTER(C.c_float), C.POINTER(AllreduceEpilogue), _p, _sz, _p]),
     "b2d_gqa_decode_ex": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                  _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _p, _sz,
                                  _p, _i64, _i64, _i32, _i32, _p]),
@@ -62,6 +68,8 @@ SIGNATURES = {
     "b2d_silu_mul": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _p]),
     "b2d_allreduce_buffer_bytes": (_sz, [_i64, _i32, _i32]),
     "b2d_allreduce": (_i32, [_p, _p, _i64, _i32, C.POINTER(C.c_void_p), _i32, _i32, _i64, _i32, _p]),
+    "b2d_allreduce_add_rmsnorm": (_i32, [C.POINTER(AllreduceEpilogue), _p, _i64, _p, _f32, _p, _i64, _i32, _i32,
+                                         _i32, _i32, _p]),
     "b2d_gqa_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                       _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32,
                                       _p, _i64, _i64, _i32, _p]),

@@ -66,11 +66,14 @@ class DecodeEngine:
 
     ``tp`` (a ``TPGroup`` of world size > 1, one process per GPU) runs the tensor-parallel mode: this
     rank keeps its NF4 shards and its KV heads, and the o_proj / down_proj outputs are all-reduced
-    inside the step's CUDA graph -- ``allreduce="peer"``: the one-shot NVLink peer-memory kernel
-    (``b2d_allreduce``), ``"nccl"``: NCCL. Requires ``fused=True``."""
+    inside the step's CUDA graph -- ``allreduce="fused"`` (batch <= 8): o_proj / down_proj push their
+    partial products to every peer from the GEMM epilogue and the next add+RMSNorm sums them (no
+    separate all-reduce launch); ``"peer"``: the one-shot NVLink peer-memory kernel
+    (``b2d_allreduce``) between the GEMM and the add+RMSNorm (also used for batch > 8 under
+    "fused"); ``"nccl"``: NCCL. All three give identical tokens. Requires ``fused=True``."""
 
     def __init__(self, model: MistralForCausalLM, batch: int, max_len: int, fused: bool = True,
-                 tp: TPGroup | None = None, allreduce: str = "peer"):
+                 tp: TPGroup | None = None, allreduce: str = "fused"):
         cfg = model.config
         self.model = model
         self.B, self.S = batch, max_len
@@ -108,10 +111,16 @@ class DecodeEngine:
         self.fused = fused
         if fused:
             self._init_fused(cfg)
-        if self.tp is not None and allreduce == "peer":
+        if allreduce not in ("fused", "peer", "nccl"):
+            raise ValueError(f"allreduce must be 'fused', 'peer' or 'nccl', got {allreduce!r}")
+        self.ar_fused = self.tp is not None and allreduce == "fused" and self.pair
+        if self.ar_fused:
+            self.tp.enable_fused_allreduce(batch, cfg.hidden_size, 2 * self.L, self.dtype, self.device)
+            for g, w in zip(self.groups, self.w):
+                g["o"] = NF4Group([w["o"]], mode="allreduce")
+                g["down"] = NF4Group([w["down"]], mode="allreduce")
+        elif self.tp is not None and allreduce in ("fused", "peer"):
             self.tp.enable_peer_allreduce(batch * cfg.hidden_size, self.dtype, self.device)
-        elif self.tp is not None and allreduce != "nccl":
-            raise ValueError(f"allreduce must be 'peer' or 'nccl', got {allreduce!r}")
 
     def _init_fused(self, cfg):
         B, dev, dt = self.B, self.device, self.dtype
@@ -149,10 +158,18 @@ class DecodeEngine:
         B, H, KVH, D = self.B, self.H, self.KVH, self.D
         PDL, STATIC = _lib.LAUNCH_PDL, _lib.LAUNCH_PDL | _lib.STATIC_WEIGHTS
         torch.index_select(m.embed_tokens.weight, 0, self.ids, out=self.r)
+        tp, arf = self.tp, self.ar_fused
         x_in = None
+
+        def norm(weight, x, site):   # residual += x (or the all-reduced partials of `site`); xn = RMSNorm
+            if site is None:
+                add_rmsnorm(self.r, weight, self.eps, self.xn, x=x, flags=PDL)
+            else:
+                tp.allreduce_add_rmsnorm(site, self.r, weight, self.eps, self.xn, flags=PDL)
+
         for i, layer in enumerate(m.layers):
             w, g = self.w[i], self.groups[i]
-            add_rmsnorm(self.r, layer.input_layernorm.weight, self.eps, self.xn, x=x_in, flags=PDL)
+            norm(layer.input_layernorm.weight, x_in, 2 * i - 1 if arf and i > 0 else None)
             if self.pair:
                 g["qkv"].matmul(self.xn, [self.q, self.k, self.v], flags=STATIC)
             else:
@@ -163,24 +180,31 @@ class DecodeEngine:
             decode_attention(q3.view(B, H, 1, D), self.k_cache[i], self.v_cache[i], self.scale, seqlens=self.seqlens,
                              out=self.attn, flags=PDL)
             a2 = self.attn.view(B, H * D)
-            if self.pair:
+            if arf:
+                g["o"].matmul(a2, flags=STATIC, epilogue=tp.epilogue(2 * i))
+            elif self.pair:
                 g["o"].matmul(a2, [self.o_out], flags=STATIC)
             else:
                 w["o"].matmul(a2, out=self.o_out)
-            if self.tp is not None:
-                self.tp.all_reduce(self.o_out)
-            add_rmsnorm(self.r, layer.post_attention_layernorm.weight, self.eps, self.xn, x=self.o_out, flags=PDL)
+            if tp is not None and not arf:
+                tp.all_reduce(self.o_out)
+            norm(layer.post_attention_layernorm.weight, self.o_out, 2 * i if arf else None)
             if self.pair:
                 g["gateup"].matmul(self.xn, [self.h_mlp], flags=STATIC)
-                g["down"].matmul(self.h_mlp, [self.down_out], flags=STATIC)
+                if arf:
+                    g["down"].matmul(self.h_mlp, flags=STATIC, epilogue=tp.epilogue(2 * i + 1))
+                else:
+                    g["down"].matmul(self.h_mlp, [self.down_out], flags=STATIC)
             else:
                 w["gate"].matmul(self.xn, out=self.g_out); w["up"].matmul(self.xn, out=self.h_mlp)
                 silu_mul(self.g_out, self.h_mlp, out=self.h_mlp, flags=PDL)
                 w["down"].matmul(self.h_mlp, out=self.down_out)
-            if self.tp is not None:
-                self.tp.all_reduce(self.down_out)
+            if tp is not None and not arf:
+                tp.all_reduce(self.down_out)
             x_in = self.down_out
-        add_rmsnorm(self.r, m.norm.weight, self.eps, self.xn, x=x_in, flags=PDL)
+        norm(m.norm.weight, x_in, 2 * self.L - 1 if arf else None)
+        if arf:
+            tp.advance()
         logits = self.model.lm_head(self.xn)                        # [B, vocab]
         self.logits.copy_(logits)
         torch.argmax(logits, -1, out=self.next_ids)

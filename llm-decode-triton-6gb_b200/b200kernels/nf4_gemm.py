@@ -20,6 +20,8 @@ Python or CPU fallback.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _lib
@@ -166,19 +168,24 @@ class NF4Group:
     ``mode="independent"``: ``outs[i] = x @ W_i^T`` (q/k/v of a decoder layer).
     ``mode="silu_mul"``: two weights of equal shape, ``out = silu(x @ W_0^T) * (x @ W_1^T)`` with the
     model-dtype rounding of a Mistral MLP (gate/up fused with the SwiGLU).
+    ``mode="allreduce"``: one weight (a row-parallel shard); the product goes to the tensor-parallel
+    peers instead of an output (``matmul(x, epilogue=...)``, summed by ``TPGroup.allreduce_add_rmsnorm``).
     Up to ``MAX_M = 8`` rows. ``flags``: ``_lib.LAUNCH_PDL | _lib.STATIC_WEIGHTS``."""
 
     MAX_M = 8
 
     def __init__(self, weights: list, mode: str = "independent"):
-        assert 1 <= len(weights) <= 4 and mode in ("independent", "silu_mul"), (len(weights), mode)
+        assert 1 <= len(weights) <= 4 and mode in ("independent", "silu_mul", "allreduce"), (len(weights), mode)
         w0 = weights[0]
         for w in weights:
             assert w.K == w0.K and w.nested == w0.nested, "segments must share K and the nested flag"
             assert torch.equal(w.code, w0.code), "segments must share the NF4 codebook"
-        self.mode = _lib.SEG_SILU_MUL if mode == "silu_mul" else _lib.SEG_INDEPENDENT
+        self.mode = {"independent": _lib.SEG_INDEPENDENT, "silu_mul": _lib.SEG_SILU_MUL,
+                     "allreduce": _lib.SEG_ALLREDUCE}[mode]
         if self.mode == _lib.SEG_SILU_MUL:
             assert len(weights) == 2 and weights[0].N == weights[1].N
+        if self.mode == _lib.SEG_ALLREDUCE:
+            assert len(weights) == 1
         self.weights = list(weights)
         self.K, self.nested = w0.K, w0.nested
         self.Ns = [w.N for w in weights]
@@ -198,10 +205,21 @@ class NF4Group:
     def nbytes(self) -> int:
         return sum(w.nbytes for w in self.weights)
 
-    def matmul(self, x: torch.Tensor, outs: list | None = None, flags: int = 0) -> list:
-        """x [M, K] (row stride multiple of 8) -> list of outputs [M, N_i] (or one for silu_mul)."""
+    def matmul(self, x: torch.Tensor, outs: list | None = None, flags: int = 0, epilogue=None) -> list:
+        """x [M, K] (row stride multiple of 8) -> list of outputs [M, N_i] (or one for silu_mul);
+        mode "allreduce": no outputs, ``epilogue`` (a ``_lib.AllreduceEpilogue``) says where to send."""
         assert x.dim() == 2 and x.shape[1] == self.K and x.stride(1) == 1, tuple(x.shape)
         M = x.shape[0]
+        if self.mode == _lib.SEG_ALLREDUCE:
+            assert epilogue is not None
+            self._segs[0].y, self._segs[0].ldy = None, self.Ns[0]
+            nbytes = _lib.load().b2d_nf4_gemm_workspace_bytes(max(M, 1), sum(self.Ns), self.K)
+            ws = gemm_workspace(x.device, nbytes)
+            dt = _lib.dtype_code(x.dtype)
+            _lib.call("b2d_nf4_gemm_multi", x.data_ptr(), x.stride(0), self._segs, 1, int(self.nested), M, self.K,
+                      dt, dt, self.mode, flags, self._code_host, C.byref(epilogue), ws.data_ptr(), ws.numel(),
+                      _lib.stream_ptr(x.device))
+            return []
         if outs is None:
             outs = [torch.empty((M, n), device=x.device, dtype=x.dtype) for n in self.n_out]
         for i, o in enumerate(outs):
@@ -212,8 +230,8 @@ class NF4Group:
         ws = gemm_workspace(x.device, nbytes)
         dt = _lib.dtype_code(x.dtype)
         _lib.call("b2d_nf4_gemm_multi", x.data_ptr(), x.stride(0), self._segs, len(self.weights), int(self.nested),
-                  M, self.K, dt, _lib.dtype_code(outs[0].dtype), self.mode, flags, self._code_host, ws.data_ptr(),
-                  ws.numel(), _lib.stream_ptr(x.device))
+                  M, self.K, dt, _lib.dtype_code(outs[0].dtype), self.mode, flags, self._code_host, None,
+                  ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device))
         return outs
 
 

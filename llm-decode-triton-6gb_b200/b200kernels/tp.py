@@ -31,15 +31,21 @@ class TPGroup:
 
     ``all_reduce`` sums a tensor over the group in place: with ``enable_peer_allreduce`` (called once,
     collectively) through ``b2d_allreduce`` -- every rank pushes its slice into its peers' memory over
-    NVLink and sums locally, one launch -- otherwise through NCCL."""
+    NVLink and sums locally, one launch -- otherwise through NCCL.
+
+    ``enable_fused_allreduce`` (collective) sets up the all-reduce fused into the row-parallel GEMM's
+    epilogue: an ``NF4Group(mode="allreduce")`` launch with ``epilogue(site)`` pushes its partial
+    product to every peer, and ``allreduce_add_rmsnorm(site, ...)`` sums the partials and applies the
+    residual add + RMSNorm that follows. Each of a step's all-reduces has its own site; ``advance()``
+    (once per step, after the last site) moves the device step counter the epochs are derived from."""
     rank: int
     world: int
     group: object = None
     _peer: object = None
+    _fused: object = None
 
-    def enable_peer_allreduce(self, n_max: int, dtype, device) -> None:
-        """Map one symmetric buffer per rank (torch symmetric memory: every peer's buffer addressable
-        from this GPU) for the one-shot all-reduce of up to ``n_max`` elements."""
+    def _symmetric_buffer(self, n_max: int, dtype, device):
+        """One zero-filled buffer per rank, mapped by every peer (torch symmetric memory)."""
         import ctypes
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
@@ -54,13 +60,55 @@ class TPGroup:
         hdl = symm_mem.rendezvous(buf, group.group_name)
         ptrs = [int(p) for p in hdl.buffer_ptrs]
         dist.barrier(group=group, device_ids=[torch.device(device).index])
-        self._peer = dict(buf=buf, hdl=hdl, n_max=int(n_max), ptrs=(ctypes.c_void_p * self.world)(*ptrs))
+        return dict(buf=buf, hdl=hdl, n_max=int(n_max), ptrs=(ctypes.c_void_p * self.world)(*ptrs))
+
+    def enable_peer_allreduce(self, n_max: int, dtype, device) -> None:
+        """Map the buffers of the one-shot all-reduce of up to ``n_max`` elements."""
+        self._peer = self._symmetric_buffer(n_max, dtype, device)
+
+    def enable_fused_allreduce(self, rows: int, cols: int, sites: int, dtype, device) -> None:
+        """Map the buffers of the GEMM-fused all-reduce of ``rows`` x ``cols`` outputs (tokens x
+        hidden) at ``sites`` points per step, with a device step counter starting at 0."""
+        from . import _lib
+        n_max = 2 * ((rows + 1) // 2) * cols
+        n_max += -n_max % 8
+        f = self._symmetric_buffer(n_max, dtype, device)
+        f["step"] = torch.zeros(1, dtype=torch.int64, device=device)
+        f["sites"] = int(sites)
+        f["eps"] = []
+        for site in range(sites):
+            e = _lib.AllreduceEpilogue()
+            e.peer_bufs, e.rank, e.world, e.n_max = f["ptrs"], self.rank, self.world, n_max
+            e.step, e.site, e.sites = f["step"].data_ptr(), site, sites
+            f["eps"].append(e)
+        self._fused = f
+
+    def epilogue(self, site: int):
+        """The ``b2d_allreduce_epilogue`` of one site (kept alive by this group)."""
+        return self._fused["eps"][site]
+
+    def allreduce_add_rmsnorm(self, site: int, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                              out: torch.Tensor, flags: int = 0) -> torch.Tensor:
+        """residual += (sum over ranks of the site's partials); out = RMSNorm(residual) * weight."""
+        import ctypes
+        from . import _lib
+        M, D = residual.shape
+        _lib.call("b2d_allreduce_add_rmsnorm", ctypes.byref(self._fused["eps"][site]), residual.data_ptr(),
+                  residual.stride(0), weight.data_ptr(), float(eps), out.data_ptr(), out.stride(0), M, D,
+                  _lib.dtype_code(residual.dtype), int(flags), _lib.stream_ptr(residual.device))
+        return out
+
+    def advance(self) -> None:
+        """Move the fused all-reduce to the next step (stream-ordered; capturable in a CUDA graph)."""
+        self._fused["step"].add_(1)
 
     def peer_errors(self) -> int:
-        """Timed-out waits recorded by the peer all-reduce on this rank (0 when healthy)."""
-        if self._peer is None:
-            return 0
-        return int(self._peer["buf"][256:260].view(torch.int32).item())
+        """Timed-out waits recorded by the peer all-reduces on this rank (0 when healthy)."""
+        n = 0
+        for b in (self._peer, self._fused):
+            if b is not None:
+                n += int(b["buf"][256:260].view(torch.int32).item())
+        return n
 
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:

@@ -158,6 +158,38 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, int rank) {
   return v;
 }
 
+// Tensor-parallel all-reduce through peer memory, flag-in-word protocol: a 64-bit word carries 32
+// bits of data (two fp16/bf16 values) in its low half and the call's epoch in its high half, written
+// with one 64-bit store, so a reader that sees the epoch also sees the data. Every rank owns one buffer
+// mapped by all peers; its words start at kArDataOff, laid out [2 epoch parities][world][words].
+constexpr size_t kArDataOff = 512;
+constexpr int kArMaxWorld = 8;
+struct ArPeers {
+  uint8_t* peer[kArMaxWorld];   // peer[p] = rank p's buffer as seen from this GPU
+  int rank, world;
+  int64_t words;                // words per rank slot
+  const int64_t* step;          // device step counter: epoch = step * sites + site + 1
+  int site, sites;
+};
+__device__ __forceinline__ uint32_t ar_epoch(const ArPeers& p) {
+  return static_cast<uint32_t>(*p.step * p.sites + p.site + 1);
+}
+// Rank `src`'s slot for epoch e in the buffer of rank `dst`.
+__device__ __forceinline__ uint64_t* ar_slot(const ArPeers& p, int dst, int src, uint32_t e) {
+  return reinterpret_cast<uint64_t*>(p.peer[dst] + kArDataOff) + (static_cast<int64_t>(e & 1) * p.world + src) * p.words;
+}
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ld_word2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];\n" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // Device-scope acquire-release atomic add (cheaper than a sequentially consistent fence + atomic):
 // writes made before it by this thread, or by threads it synchronised with through a barrier, are
 // visible to whoever observes the new value; reads after it see what earlier releasers published.

@@ -88,6 +88,109 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T* x, i
   }
 }
 
+// ------------------------------------------------------------------ all-reduce consumer + add + RMSNorm
+// The partials of a GEMM with the all-reduce epilogue arrive as flag-in-word words, word
+// (t / 2) * D + n holding tokens t, t + 1 (t even) of column n. One CTA per token pair; thread tid
+// owns the same 8-column chunks as in add_rmsnorm_kernel, and every sum is formed in the same order
+// (peers in rank order; squares per thread, then warps, then the CTA), so the result has the bits of
+// b2d_allreduce followed by b2d_add_rmsnorm.
+// Polls a thread makes in one launch before it gives up on its peers (about a second); once a rank
+// has recorded an error, later launches poll once and return, so a missing peer costs one timeout.
+constexpr long long kArConsumerSpin = 1LL << 22;
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) allreduce_add_rmsnorm_kernel(const ArPeers a, T* res, int64_t ldr,
+                                                                             const T* weight, float eps, T* out,
+                                                                             int64_t ldo, int M, int D) {
+  pdl_launch_dependents();
+  __shared__ float s_part[2][kNormThreads / 32];
+  const int tp = blockIdx.x, tid = threadIdx.x;
+  const int nchunk = D / 8;
+  const bool two = 2 * tp + 1 < M;
+  uint4 wq[kNormMaxChunks];
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const int ci = tid + c * kNormThreads;
+    if (ci < nchunk) wq[c] = __ldg(reinterpret_cast<const uint4*>(weight + ci * 8));
+  }
+  pdl_wait();   // the epoch counter and the residual belong to the stream order from here on
+  const uint32_t e = ar_epoch(a);
+  int* errors = reinterpret_cast<int*>(a.peer[a.rank] + 256);
+  long long budget = *reinterpret_cast<volatile int*>(errors) == 0 ? kArConsumerSpin : 0;
+  float h[2][kNormMaxChunks][8];
+  float ss[2] = {0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const int ci = tid + c * kNormThreads;
+    if (ci < nchunk) {
+      float x[2][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[0][i] = x[1][i] = 0.f;
+      for (int p = 0; p < a.world; ++p) {
+        const uint64_t* q = ar_slot(a, a.rank, p, e) + static_cast<int64_t>(tp) * D + ci * 8;
+        uint64_t w[8];
+        for (;;) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ld_word2(q + 2 * j, w[2 * j], w[2 * j + 1]);
+          bool ok = true;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ok &= static_cast<uint32_t>(w[j] >> 32) == e;
+          if (ok || budget <= 0) break;
+          if (--budget == 0) {
+            atomicAdd(errors, 1);
+            break;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t d = static_cast<uint32_t>(w[j]);
+          const T* hv = reinterpret_cast<const T*>(&d);
+          x[0][j] += Dt<T>::to_f32(hv[0]);
+          x[1][j] += Dt<T>::to_f32(hv[1]);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t == 1 && !two) break;
+        const int64_t row = 2 * tp + t;
+        unpack8<T>(*reinterpret_cast<const uint4*>(res + row * ldr + ci * 8), h[t][c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[t][c][i] = rnd<T>(h[t][c][i] + rnd<T>(x[t][i]));   // residual + all-reduced
+        *reinterpret_cast<uint4*>(res + row * ldr + ci * 8) = pack8<T>(h[t][c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss[t] = fmaf(h[t][c][i], h[t][c][i], ss[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+    if ((tid & 31) == 0) s_part[t][tid >> 5] = ss[t];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (t == 1 && !two) break;
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += s_part[t][w];
+    const float rstd = rsqrtf(tot / static_cast<float>(D) + eps);
+    const int64_t row = 2 * tp + t;
+#pragma unroll
+    for (int c = 0; c < kNormMaxChunks; ++c) {
+      const int ci = tid + c * kNormThreads;
+      if (ci < nchunk) {
+        float wv[8], o[8];
+        unpack8<T>(wq[c], wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = wv[i] * rnd<T>(h[t][c][i] * rstd);
+        *reinterpret_cast<uint4*>(out + row * ldo + ci * 8) = pack8<T>(o);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ rotary embedding + KV append
 struct RopeArgs {
   const void* q; int64_t ldq;
@@ -203,6 +306,43 @@ extern "C" int b2d_add_rmsnorm(const void* x, int64_t ldx, void* residual, int64
   return launch_kernel(add_rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(kNormThreads), 0, s, pdl,
                        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<__nv_bfloat16*>(residual), ldr,
                        static_cast<const __nv_bfloat16*>(weight), eps, static_cast<__nv_bfloat16*>(out), ldo, D);
+}
+
+extern "C" int b2d_allreduce_add_rmsnorm(const b2d_allreduce_epilogue* ar, void* residual, int64_t ldr,
+                                         const void* weight, float eps, void* out, int64_t ldo, int M, int D,
+                                         int dtype, int flags, void* stream) {
+  if (!ar || M < 0 || D < 0) return B2D_ERR_ARG;
+  if (dtype != B2D_F16 && dtype != B2D_BF16) return B2D_ERR_DTYPE;
+  if (!ar->peer_bufs || !ar->step || ar->world < 1 || ar->world > kArMaxWorld || ar->rank < 0 ||
+      ar->rank >= ar->world || ar->sites < 1 || ar->site < 0 || ar->site >= ar->sites || ar->n_max % 8)
+    return B2D_ERR_ARG;
+  if (D % 8 != 0 || D > kNormThreads * 8 * kNormMaxChunks) return B2D_ERR_SHAPE;
+  if (static_cast<int64_t>((M + 1) / 2) * D > ar->n_max / 2) return B2D_ERR_SHAPE;
+  if (M == 0 || D == 0) return B2D_OK;
+  if (!residual || !weight || !out) return B2D_ERR_ARG;
+  if (ldr < D || ldo < D) return B2D_ERR_SHAPE;
+  if (!aligned(residual, 16) || !aligned(weight, 16) || !aligned(out, 16) || ldr % 8 || ldo % 8)
+    return B2D_ERR_ALIGN;
+  ArPeers a{};
+  for (int p = 0; p < ar->world; ++p) {
+    if (!ar->peer_bufs[p] || !aligned(ar->peer_bufs[p], 256)) return B2D_ERR_ALIGN;
+    a.peer[p] = static_cast<uint8_t*>(ar->peer_bufs[p]);
+  }
+  a.rank = ar->rank; a.world = ar->world; a.words = ar->n_max / 2;
+  a.step = ar->step; a.site = ar->site; a.sites = ar->sites;
+  DeviceInfo di;
+  int st;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid((M + 1) / 2);
+  if (dtype == B2D_F16)
+    return launch_kernel(allreduce_add_rmsnorm_kernel<__half>, grid, dim3(kNormThreads), 0, s, pdl, a,
+                         static_cast<__half*>(residual), ldr, static_cast<const __half*>(weight), eps,
+                         static_cast<__half*>(out), ldo, M, D);
+  return launch_kernel(allreduce_add_rmsnorm_kernel<__nv_bfloat16>, grid, dim3(kNormThreads), 0, s, pdl, a,
+                       static_cast<__nv_bfloat16*>(residual), ldr, static_cast<const __nv_bfloat16*>(weight), eps,
+                       static_cast<__nv_bfloat16*>(out), ldo, M, D);
 }
 
 extern "C" int b2d_rope_kv_append(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,

@@ -25,6 +25,8 @@
 //  * The MMA reduction dimension is permuted so that each thread's 8 bytes of a block row are
 //    contiguous in memory and the matching 16 activations are contiguous too:
 //    thread (g, t) at k-step s owns bytes 8t+2s, 8t+2s+1 of its block row = k offsets 16t+4s+{0..3}.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace b2d {
@@ -74,6 +76,8 @@ struct GemmArgs {
   int static_w;              // 1: weights may be read before the preceding kernel completes
   int code_by_value;         // 1: code_v holds segment 0's 16 codebook values (no device read)
   float code_v[16];
+  int ar;                    // 1: the output goes to every peer as all-reduce words (tensor parallel)
+  ArPeers are;
   int seg_end[kMaxSeg];      // exclusive end (in row groups) of each segment
   SegView seg[kMaxSeg];
 };
@@ -248,8 +252,40 @@ __device__ __forceinline__ OT silu_mul(float gate, float up) {
 // store_group for segmented launches (32-row groups): plain segments write their own output; in
 // paired mode tile 0 holds rows of segment 0 and tile 1 the same rows of segment 1, and the
 // output (segment 0's y) receives silu(tile 0) * tile 1.
+// Epilogue kinds of the pipelined kernel, one instantiation each (an epilogue's code and registers
+// stay out of the other launches).
+constexpr int kEpiStore = 0, kEpiAllReduce = 1;
+
+// All-reduce epilogue (one segment): the partial output rounded to OT, written as flag-in-word words
+// (two tokens of one row per word: word (t/2)*N + row) into this rank's slot of every peer's buffer;
+// the consumer (b2d_allreduce_add_rmsnorm) sums the world's slots.
 template <typename OT, int NT>
-__device__ __forceinline__ void store_seg(const GemmArgs& a, int grp, const float (&v)[2][NT][4], int g, int tq) {
+__device__ __forceinline__ void store_allreduce(const GemmArgs& a, int grp, const float (&v)[2][NT][4], int g, int tq,
+                                                uint32_t e) {
+  const int64_t base = static_cast<int64_t>(grp) * 32 + g;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tp = nt * 4 + tq;   // token pair (2tp, 2tp + 1)
+    if (2 * tp >= a.M) continue;
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t w = tp * static_cast<int64_t>(a.N) + base + rt * 16 + h * 8;
+        const uint64_t word = (static_cast<uint64_t>(e) << 32) |
+                              Dt<OT>::pack2(v[rt][nt][2 * h], v[rt][nt][2 * h + 1]);
+        for (int p = 0; p < a.are.world; ++p) st_word(ar_slot(a.are, p, a.are.rank, e) + w, word);
+      }
+  }
+}
+
+template <typename OT, int NT, int EPI = kEpiStore>
+__device__ __forceinline__ void store_seg(const GemmArgs& a, int grp, const float (&v)[2][NT][4], int g, int tq,
+                                          uint32_t epoch = 0) {
+  if constexpr (EPI == kEpiAllReduce) {
+    if constexpr (!std::is_same<OT, float>::value) store_allreduce<OT, NT>(a, grp, v, g, tq, epoch);
+    return;
+  }
   if (a.pair) {
     OT* y = static_cast<OT*>(a.seg[0].y);
     const int64_t ldy = a.seg[0].ldy;
@@ -636,10 +672,10 @@ constexpr size_t pipe_smem_bytes() {
 // held by one CTA is stored at once, a group split between CTAs of the cluster is left in part[] and,
 // after a cluster barrier, the first CTA holding it adds the others' parts (distributed shared
 // memory, in rank order) and stores it. A second barrier keeps every CTA's part[] alive until read.
-template <typename OT, int NT, int NW>
+template <typename OT, int NT, int NW, int EPI>
 __device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* slots, float* part, const int* s_wa,
                                                 const int* s_wb, const int* s_fg, int A, int B, int U0, int n,
-                                                int q, int cs, int warp, int lane, int g, int tq) {
+                                                int q, int cs, int warp, int lane, int g, int tq, uint32_t epoch) {
   constexpr int E = 2 * NT * 128;
   const int upg = a.upg;
   const int gA = A / upg, gB = B > A ? (B - 1) / upg : gA - 1;
@@ -663,7 +699,7 @@ __device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* 
         }
     }
     if (!shared) {
-      store_seg<OT, NT>(a, grp, v, g, tq);
+      store_seg<OT, NT, EPI>(a, grp, v, g, tq, epoch);
       continue;
     }
     float* d = part + (grp == gA ? 0 : 1) * E + lane * 4;
@@ -703,13 +739,13 @@ __device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* 
             v[rt][nt][0] += t.x; v[rt][nt][1] += t.y; v[rt][nt][2] += t.z; v[rt][nt][3] += t.w;
           }
       }
-      store_seg<OT, NT>(a, grp, v, g, tq);
+      store_seg<OT, NT, EPI>(a, grp, v, g, tq, epoch);
     }
   }
   cluster_sync();
 }
 
-template <typename T, typename OT, int NT, bool NESTED, int NW, int R>
+template <typename T, typename OT, int NT, bool NESTED, int NW, int R, int EPI>
 __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArgs a) {
   constexpr int RT = 2;
   constexpr int E = RT * NT * 128;
@@ -775,6 +811,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
   if (NESTED) cp_async_wait<R - 2>();   // this thread's code2 copies (group 0) have landed
   __syncthreads();
   pdl_wait();   // x, the workspace and the outputs belong to the stream order from here on
+  const uint32_t epoch = EPI == kEpiAllReduce ? ar_epoch(a.are) : 0u;
 
   if (wa < wb) {
     float acc[RT][NT][4];
@@ -830,7 +867,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
       __syncwarp();   // every lane is done with the stage before it is refilled
       st_c = st_c + 1 == R ? 0 : st_c + 1;
       if (++cun == upg) {
-        if (cgrp * upg >= wa) store_seg<OT, NT>(a, cgrp, acc, g, tq);
+        if (cgrp * upg >= wa) store_seg<OT, NT, EPI>(a, cgrp, acc, g, tq, epoch);
         else park(cgrp);
         zero_acc(acc);
         cun = 0;
@@ -850,7 +887,7 @@ __global__ void __launch_bounds__(NW * 32, 1) nf4_gemm_pipe_kernel(const GemmArg
   }
   cp_async_wait<0>();
   __syncthreads();
-  combine_cluster<OT, NT, NW>(a, slots, part, s_wa, s_wb, s_fg, A, B, U0, n_cl, q, cs, warp, lane, g, tq);
+  combine_cluster<OT, NT, NW, EPI>(a, slots, part, s_wa, s_wb, s_fg, A, B, U0, n_cl, q, cs, warp, lane, g, tq, epoch);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -995,9 +1032,9 @@ struct PipeLaunch {
   int cs, ncl;
 };
 
-template <typename T, typename OT, bool NESTED, int NW, int R>
+template <typename T, typename OT, bool NESTED, int NW, int R, int EPI>
 int launch_pipe(const GemmArgs& a, bool pdl, cudaStream_t stream) {
-  auto kern = nf4_gemm_pipe_kernel<T, OT, 1, NESTED, NW, R>;
+  auto kern = nf4_gemm_pipe_kernel<T, OT, 1, NESTED, NW, R, EPI>;
   constexpr size_t smem = pipe_smem_bytes<NW, R, 1>();
   constexpr int kSizes[4] = {1, 2, 4, 8};
   static int max_clusters[64][4] = {};   // per device and size; 0 = not queried yet, -1 = unavailable
@@ -1058,16 +1095,26 @@ int launch_pipe(const GemmArgs& a, bool pdl, cudaStream_t stream) {
   return launch_status();
 }
 
+template <typename T, typename OT, int EPI>
+int dispatch_pipe_epi(const GemmArgs& a, int nested, bool pdl, cudaStream_t s) {
+  return nested ? launch_pipe<T, OT, true, B2D_PIPE_NW, B2D_PIPE_RING, EPI>(a, pdl, s)
+                : launch_pipe<T, OT, false, B2D_PIPE_NW, B2D_PIPE_RING, EPI>(a, pdl, s);
+}
+
 template <typename T, typename OT>
 int dispatch_pipe(const GemmArgs& a, int nested, bool pdl, cudaStream_t s) {
-  return nested ? launch_pipe<T, OT, true, B2D_PIPE_NW, B2D_PIPE_RING>(a, pdl, s)
-                : launch_pipe<T, OT, false, B2D_PIPE_NW, B2D_PIPE_RING>(a, pdl, s);
+  if (a.ar) {
+    if constexpr (std::is_same<OT, float>::value) return B2D_ERR_DTYPE;
+    else return dispatch_pipe_epi<T, OT, kEpiAllReduce>(a, nested, pdl, s);
+  }
+  return dispatch_pipe_epi<T, OT, kEpiStore>(a, nested, pdl, s);
 }
 
 template <typename T, typename OT, int CB, bool NESTED>
 int dispatch_tc_cb(const GemmArgs& a, const GemmConfig& c, cudaStream_t s) {
 #ifndef B2D_PIPE_OFF
-  if (CB == 4 && c.nt == 1 && c.rt == 2) return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING>(a, false, s);
+  if (CB == 4 && c.nt == 1 && c.rt == 2)
+    return launch_pipe<T, OT, NESTED, B2D_PIPE_NW, B2D_PIPE_RING, kEpiStore>(a, false, s);
 #endif
   if (c.nt == 1)
     return c.rt == 2 ? launch_tc<T, OT, 2, 1, CB, NESTED, 10>(a, c.grid, s)
@@ -1204,20 +1251,33 @@ extern "C" int b2d_nf4_gemv_simt(const void* x, int64_t ldx, const uint8_t* pack
 // decoder layer). No counterpart in the reference, which launches one kernel per projection.
 extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segment* segs, int nseg, int nested,
                                   int M, int K, int dtype, int y_dtype, int mode, int flags, const float* code_host,
-                                  void* workspace, size_t workspace_bytes, void* stream) {
+                                  const void* epilogue, void* workspace, size_t workspace_bytes, void* stream) {
   if (!segs || nseg < 1 || nseg > kMaxSeg || M < 0 || K < 0) return B2D_ERR_ARG;
-  if (mode != B2D_SEG_INDEPENDENT && mode != B2D_SEG_SILU_MUL) return B2D_ERR_ARG;
+  if (mode != B2D_SEG_INDEPENDENT && mode != B2D_SEG_SILU_MUL && mode != B2D_SEG_ALLREDUCE) return B2D_ERR_ARG;
   const bool pair = mode == B2D_SEG_SILU_MUL;
+  const bool ar = mode == B2D_SEG_ALLREDUCE;
   if (pair && (nseg != 2 || segs[0].N != segs[1].N || y_dtype != dtype)) return B2D_ERR_SHAPE;
+  const b2d_allreduce_epilogue* are = static_cast<const b2d_allreduce_epilogue*>(epilogue);
+  if (ar) {
+    if (!are || !are->peer_bufs || !are->step || are->world < 1 || are->world > kArMaxWorld || are->rank < 0 ||
+        are->rank >= are->world || are->sites < 1 || are->site < 0 || are->site >= are->sites || are->n_max % 8)
+      return B2D_ERR_ARG;
+    if (nseg != 1 || y_dtype != dtype) return B2D_ERR_SHAPE;
+    if (static_cast<int64_t>((M + 1) / 2) * segs[0].N > are->n_max / 2) return B2D_ERR_SHAPE;
+    for (int p = 0; p < are->world; ++p)
+      if (!are->peer_bufs[p] || !aligned(are->peer_bufs[p], 256)) return B2D_ERR_ALIGN;
+  }
   int64_t n_total = 0;
   for (int i = 0; i < nseg; ++i) {
     const b2d_nf4_segment& sg = segs[i];
     if (sg.N < 0) return B2D_ERR_ARG;
     if (sg.N % (pair ? 16 : 32) != 0) return B2D_ERR_SHAPE;
     // x, y, code and the shared constraints are checked per segment by the single-weight rules
+    // outputs: a paired launch writes segment 0's y; an all-reduce launch writes the peers' buffers
+    const void* yy = ar ? are->peer_bufs[are->rank] : (pair && i == 1 ? segs[0].y : sg.y);
+    const int64_t ly = ar ? sg.N : (pair && i == 1 ? segs[0].ldy : sg.ldy);
     int st = check_weight_args(x, ldx, sg.packed, sg.ld_packed, sg.absmax, sg.ld_absmax, nested, sg.code2, sg.absmax2,
-                               segs[0].code, pair && i == 1 ? segs[0].y : sg.y, pair && i == 1 ? segs[0].ldy : sg.ldy,
-                               M, sg.N, K, dtype, y_dtype, 8);
+                               segs[0].code, yy, ly, M, sg.N, K, dtype, y_dtype, 8);
     if (st != B2D_OK) return st;
     if (!chunk4_ok(K, sg.absmax, sg.ld_absmax, nested, sg.gblk_base, sg.gblk_row_stride)) return B2D_ERR_ALIGN;
     n_total += sg.N;
@@ -1243,6 +1303,16 @@ extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segm
   a.nseg = nseg;
   a.pair = pair ? 1 : 0;
   a.static_w = (flags & B2D_STATIC_WEIGHTS) ? 1 : 0;
+  if (ar) {
+    a.ar = 1;
+    for (int p = 0; p < are->world; ++p) a.are.peer[p] = static_cast<uint8_t*>(are->peer_bufs[p]);
+    a.are.rank = are->rank;
+    a.are.world = are->world;
+    a.are.words = are->n_max / 2;
+    a.are.step = are->step;
+    a.are.site = are->site;
+    a.are.sites = are->sites;
+  }
   if (code_host) {
     a.code_by_value = 1;
     for (int i = 0; i < 16; ++i) a.code_v[i] = code_host[i];

@@ -1,5 +1,6 @@
-"""GPU (2 GPUs): tensor-parallel decode (NCCL all-reduce after o_proj and down_proj) against the
-single-GPU engine and the stock HF greedy path. Skipped on a machine with fewer than 2 GPUs."""
+"""GPU (2 GPUs): tensor-parallel decode (all-reduce after o_proj and down_proj: fused into the GEMM
+epilogue, the peer-memory kernel, or NCCL) against the single-GPU engine and the stock HF greedy path.
+Skipped on a machine with fewer than 2 GPUs."""
 import json
 import os
 import socket
@@ -30,11 +31,13 @@ def test_tp2_decode_matches_single_gpu():
     assert res.returncode == 0 and line, res.stdout[-2000:] + res.stderr[-4000:]
     ranks = json.loads(line[0].split(" ", 1)[1])
     for r in ranks:
-        for mode in ("peer", "nccl"):
+        for mode in ("fused", "peer", "nccl"):
             m = r[mode]
             assert m["max_rel_logit_diff_vs_1gpu"] < 2e-2, (mode, r)
             assert m["argmax_agree_vs_1gpu"] >= 0.9, (mode, r)
             assert m["greedy_equal_stock"], (mode, r)
             assert m["peer_errors"] == 0, (mode, r)
+        # the fused all-reduce sums the same rounded partials in the same order as the peer kernel
+        assert r["fused"]["logits_sha"] == r["peer"]["logits_sha"], r
     # the peer all-reduce gives every rank identical sums, so identical logits
-    assert len({r["peer"]["logits_sum"] for r in ranks}) == 1, ranks
+    assert len({r["peer"]["logits_sha"] for r in ranks}) == 1, ranks

@@ -1,8 +1,10 @@
 """One rank of the tensor-parallel decode check (launched by tests/test_tp_gpu.py under
 torch.distributed.run, one process per GPU, NCCL). Every rank builds the same seeded model, decodes
 with its shards (all-reduce after o_proj and down_proj, captured in the CUDA graph) and compares the
-teacher-forced logits with the unsharded engine on its own GPU. Rank 0 prints one JSON line."""
+teacher-forced logits with the unsharded engine on its own GPU, for each all-reduce mode (fused into
+the GEMM epilogue, peer kernel, NCCL). Rank 0 prints one JSON line."""
 import datetime
+import hashlib
 import json
 import os
 import sys
@@ -33,7 +35,7 @@ def main():
         one = dec.DecodeEngine(model, B, 64)
         p_one, l_one = one.teacher_forced(ids, stock)
         res = {"rank": rank, "world": world}
-        for mode in ("peer", "nccl"):
+        for mode in ("fused", "peer", "nccl"):
             grp = TPGroup(rank, world)
             tp_eng = dec.DecodeEngine(model, B, 64, tp=grp, allreduce=mode)
             p_tp, l_tp = tp_eng.teacher_forced(ids, stock)
@@ -43,7 +45,8 @@ def main():
             res[mode] = {"max_rel_logit_diff_vs_1gpu": (l_tp - l_one).abs().max().item() / l_one.abs().max().item(),
                          "argmax_agree_vs_1gpu": (p_tp == p_one).float().mean().item(),
                          "greedy_equal_stock": bool(torch.equal(ours, stock)), "peer_errors": grp.peer_errors(),
-                         "logits_sum": float(l_tp.double().sum())}
+                         "logits_sum": float(l_tp.double().sum()),
+                         "logits_sha": hashlib.sha256(l_tp.float().cpu().numpy().tobytes()).hexdigest()}
             dist.barrier(device_ids=[dev.index])
         out = [None] * world
         dist.all_gather_object(out, res)
