@@ -149,6 +149,12 @@ __device__ __forceinline__ int cluster_count() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
+// Cluster barrier without memory ordering: only says that every thread of the cluster got here (used
+// to keep a CTA's shared memory alive until remote readers, whose loaded values are already consumed,
+// are done with it).
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.aligned;\n" ::: "memory");
+}
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, int rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(local_addr), "r"(rank));

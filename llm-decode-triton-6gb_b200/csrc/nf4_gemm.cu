@@ -710,6 +710,7 @@ __device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* 
         *reinterpret_cast<float4*>(d + (rt * NT + nt) * 128) =
             make_float4(v[rt][nt][0], v[rt][nt][1], v[rt][nt][2], v[rt][nt][3]);
   }
+  if (cs == 1) return;   // a lone CTA holds its groups whole: nothing is shared, no cluster barrier
   cluster_sync();
   // owners: warp 0 takes the CTA's first group, warp 1 its last (when shared and first held here)
   if (warp < 2 && span > 0) {
@@ -742,7 +743,9 @@ __device__ __forceinline__ void combine_cluster(const GemmArgs& a, const float* 
       store_seg<OT, NT, EPI>(a, grp, v, g, tq, epoch);
     }
   }
-  cluster_sync();
+  // keeps this CTA's part[] alive until the owners have read it; their loaded values are consumed
+  // (stored) before they arrive, so the barrier needs no memory ordering
+  cluster_sync_relaxed();
 }
 
 template <typename T, typename OT, int NT, bool NESTED, int NW, int R, int EPI>
