@@ -285,7 +285,7 @@ def run_b200(args):
     per_layer = (5 + 4) if eng.pair else (5 + 7 + 1)
     if tp is not None and not eng.ar_fused:   # fused: the GEMMs push, the add+RMSNorm launches sum
         per_layer += 2
-    launches_per_step = args.layers * per_layer + 1
+    launches_per_step = args.layers * per_layer + 1 + (1 if eng.lm_fused else 0)   # + final norm (+ lm_head)
 
     cpu = None
     if world == 1 and rank == 0:   # the reference CPU path on the host, at N=1 only

@@ -269,6 +269,23 @@ int b2d_rope_kv_append(const void* q, int64_t ldq, const void* k, int64_t ldk, c
 int b2d_silu_mul(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo,
                  int M, int N, int dtype, int flags, void* stream);
 
+/* ================================================================ lm_head + greedy argmax
+ * logits[m, v] = x[m, :] . W[v, :] (fp32 accumulation, rounded to dtype) and ids[m] = the index of the
+ * largest logit of row m, ties to the lowest index -- replaces the reference decode step's
+ * `lm_head` GEMV followed by `logits.argmax(-1)` (profiling/common.py decode_step; the stock
+ * LlamaForCausalLM/MistralForCausalLM head) with one launch. W is the [V, K] row-major head weight
+ * (row stride ldw), x [M, K]; 1 <= M <= 8, K % 256 == 0, 16-byte aligned x and W, ldx/ldw % 8 == 0.
+ * Outputs (any may be NULL, not all): logits [M, V] (row stride ld_logits), ids int64 [M], keys [M] =
+ * the packed (value, index) maxima, ordered as signed 64-bit integers -- for a vocabulary-parallel
+ * shard, indices are offset by vocab_offset and the shards' results merge by taking the maximum key
+ * over ranks (id = 0xFFFFFFFF - (key & 0xFFFFFFFF)). Workspace: b2d_lm_head_workspace_bytes(V) bytes,
+ * 256-byte aligned, zero-filled once before first use (it returns to zero after every call); calls
+ * sharing a workspace must not overlap. flags: B2D_LAUNCH_PDL | B2D_STATIC_WEIGHTS. */
+size_t b2d_lm_head_workspace_bytes(int V);
+int b2d_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int V, int K,
+                       int64_t vocab_offset, void* logits, int64_t ld_logits, int64_t* ids, long long* keys,
+                       int dtype, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ================================================================ tensor-parallel all-reduce
  * One-shot sum of n elements across `world` GPUs over NVLink peer memory (no counterpart in the
  * reference, which is single-GPU; used in place of the NCCL all-reduce after o_proj and down_proj).

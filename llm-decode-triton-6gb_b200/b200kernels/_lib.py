@@ -68,6 +68,9 @@ SIGNATURES = {
     "b2d_silu_mul": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _p]),
     "b2d_allreduce_buffer_bytes": (_sz, [_i64, _i32, _i32]),
     "b2d_allreduce": (_i32, [_p, _p, _i64, _i32, C.POINTER(C.c_void_p), _i32, _i32, _i64, _i32, _p]),
+    "b2d_lm_head_workspace_bytes": (_sz, [_i32]),
+    "b2d_lm_head_argmax": (_i32, [_p, _i64, _p, _i64, _i32, _i32, _i32, _i64, _p, _i64, _p, _p, _i32, _i32, _p, _sz,
+                                  _p]),
     "b2d_allreduce_add_rmsnorm": (_i32, [C.POINTER(AllreduceEpilogue), _p, _i64, _p, _f32, _p, _i64, _i32, _i32,
                                          _i32, _i32, _p]),
     "b2d_gqa_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,

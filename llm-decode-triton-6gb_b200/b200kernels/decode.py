@@ -11,7 +11,10 @@ with per-sequence lengths and captures one whole decode step (32 layers) in a CU
 * attention -> ``decode_attention`` (split-K partial + log-sum-exp combine);
 * the glue ops (residual add + RMSNorm, rotary embedding + KV append) -> this library's kernels
   (``fused=True``), every launch a programmatic dependent of the previous one; or the HF modules
-  themselves (``fused=False``). Embedding, lm_head and argmax stay torch ops.
+  themselves (``fused=False``);
+* lm_head + argmax -> one ``lm_head_argmax`` launch at batch <= 8 (fused mode; vocabulary-parallel
+  under tensor parallelism, the shards' maxima merged by one all-gather of 8-byte keys); otherwise
+  torch ops. The embedding stays a torch op.
 
 Prompts are prefilled through the HF forward (the reference's prefill path: SDPA, and dequant +
 library GEMM for the many-row linears); the prompt's K/V are then copied into the static cache.
@@ -26,6 +29,7 @@ from transformers.models.mistral.modeling_mistral import apply_rotary_pos_emb
 from . import _lib
 from .decode_attention import decode_attention
 from .glue import add_rmsnorm, rope_kv_append, silu_mul
+from .lm_head import MAX_M as LM_MAX_M, lm_head_argmax, merge_keys
 from .linear4bit import quantize_model_linears
 from .nf4_gemm import NF4Group, NF4Weight
 from .tp import TPGroup, local_heads, shard_layer
@@ -121,6 +125,21 @@ class DecodeEngine:
                 g["down"] = NF4Group([w["down"]], mode="allreduce")
         elif self.tp is not None and allreduce in ("fused", "peer"):
             self.tp.enable_peer_allreduce(batch * cfg.hidden_size, self.dtype, self.device)
+        head = model.lm_head
+        self.lm_fused = (fused and batch <= LM_MAX_M and head.bias is None and head.weight.dtype == self.dtype
+                         and cfg.hidden_size % 256 == 0
+                         and (self.tp is None or cfg.vocab_size % self.tp.world == 0))
+        if self.lm_fused:
+            V = cfg.vocab_size
+            if self.tp is None:
+                self.lm_w, self.lm_off = head.weight.detach().contiguous(), 0
+            else:   # vocabulary-parallel: this rank's rows of the head
+                Vl = V // self.tp.world
+                self.lm_off = self.tp.rank * Vl
+                self.lm_w = head.weight.detach()[self.lm_off:self.lm_off + Vl].contiguous()
+                self.logits_local = torch.zeros(batch, Vl, dtype=self.dtype, device=self.device)
+                self.keys = torch.zeros(batch, dtype=torch.int64, device=self.device)
+                self.keys_all = torch.zeros(self.tp.world * batch, dtype=torch.int64, device=self.device)
 
     def _init_fused(self, cfg):
         B, dev, dt = self.B, self.device, self.dtype
@@ -205,9 +224,18 @@ class DecodeEngine:
         norm(m.norm.weight, x_in, 2 * self.L - 1 if arf else None)
         if arf:
             tp.advance()
-        logits = self.model.lm_head(self.xn)                        # [B, vocab]
-        self.logits.copy_(logits)
-        torch.argmax(logits, -1, out=self.next_ids)
+        if self.lm_fused and tp is None:
+            lm_head_argmax(self.xn, self.lm_w, logits=self.logits, ids=self.next_ids, flags=STATIC)
+        elif self.lm_fused:
+            import torch.distributed as dist
+            lm_head_argmax(self.xn, self.lm_w, logits=self.logits_local, keys=self.keys, vocab_offset=self.lm_off,
+                           flags=STATIC)
+            dist.all_gather_into_tensor(self.keys_all, self.keys, group=tp.group)
+            merge_keys(self.keys_all.view(tp.world, B), out=self.next_ids)
+        else:
+            logits = self.model.lm_head(self.xn)                        # [B, vocab]
+            self.logits.copy_(logits)
+            torch.argmax(logits, -1, out=self.next_ids)
         self.ids.copy_(self.next_ids)
         self.pos.add_(1)
 
@@ -298,6 +326,18 @@ class DecodeEngine:
         self.pos.fill_(context)
         self.ids.random_(0, self.model.config.vocab_size, generator=g)
 
+    def full_logits(self) -> torch.Tensor:
+        """The last step's logits [B, vocab]. Under tensor parallelism with the vocabulary-parallel
+        head, every rank holds its slice and this gathers them (a collective: all ranks call it)."""
+        if self.tp is None or not self.lm_fused:
+            return self.logits
+        import torch.distributed as dist
+        W, (B, Vl) = self.tp.world, self.logits_local.shape
+        buf = torch.empty(W * B, Vl, dtype=self.dtype, device=self.device)
+        dist.all_gather_into_tensor(buf, self.logits_local, group=self.tp.group)
+        self.logits.copy_(buf.view(W, B, Vl).permute(1, 0, 2).reshape(B, W * Vl))
+        return self.logits
+
     @torch.inference_mode()
     def teacher_forced(self, prompt_ids: torch.Tensor, tokens: torch.Tensor):
         """Decode consuming the given tokens [B, T] (instead of our own argmax): returns our argmax
@@ -309,7 +349,7 @@ class DecodeEngine:
         for t in range(1, tokens.shape[1]):
             self.ids.copy_(tokens[:, t - 1])
             preds.append(self.step().clone())
-            logits.append(self.logits.float())
+            logits.append(self.full_logits().float())
         return torch.stack(preds, 1), torch.stack(logits, 1)
 
     @torch.inference_mode()
