@@ -205,6 +205,16 @@ def run_b200(args):
         eng.prefill(prompts.to(dev))
     eng.capture()
     clk = ClockSampler(dev.index).start()
+    # keep the GPU busy until nvidia-smi reports (its start-up takes ~1 s); every rank takes the same
+    # number of steps (the ranks agree on "not ready" through a max over ranks)
+    t_wait = time.perf_counter()
+    while True:
+        waiting = clk.proc is not None and not clk.lines and time.perf_counter() - t_wait < 15
+        if _max_over_ranks(1.0 if waiting else 0.0, world, dev) == 0.0:
+            break
+        for _ in range(8):
+            eng.step()
+        torch.cuda.synchronize(dev)
     for _ in range(W):
         eng.step()
     _barrier(world, dev)
