@@ -406,6 +406,25 @@ def run_kernels(args):
                       flush=True)
             del ws
             torch.cuda.empty_cache()
+    elif args.kernel == "lm_head":   # Mistral-7B head 32000x4096 fp16 + argmax (two weight copies > 2x L2)
+        from b200kernels.lm_head import lm_head_argmax
+        V, K = 32000, 4096
+        ws = [(torch.randn(V, K, generator=torch.Generator().manual_seed(c)) * 0.02).half().to(dev)
+              for c in range(1 if args.profile_iters else 2)]
+        for M in batches:
+            x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().to(dev)
+            lg = torch.empty(M, V, dtype=torch.half, device=dev)
+            ids = torch.empty(M, dtype=torch.int64, device=dev)
+            if args.profile_iters:
+                for _ in range(args.profile_iters):
+                    lm_head_argmax(x, ws[0], logits=lg, ids=ids)
+                torch.cuda.synchronize()
+                continue
+            us = _graph_time_us([lambda w=w: lm_head_argmax(x, w, logits=lg, ids=ids) for w in ws])
+            nbytes = V * K * 2 + M * K * 2 + M * V * 2
+            print(json.dumps({"kernel": "lm_head_argmax", "V": V, "K": K, "M": M, "us": round(us, 2),
+                              "GBps": round(nbytes / us / 1e3, 1), "pct_peak": round(100 * nbytes / us / 1e3 / peak, 1),
+                              "peak_kind": peak_kind}), flush=True)
     else:
         contexts = [int(s) for s in args.contexts.split(",")]
         for B in batches:
@@ -435,7 +454,7 @@ def run_kernels(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["nf4", "attention"], default=None,
+    ap.add_argument("--kernel", choices=["nf4", "attention", "lm_head"], default=None,
                     help="kernel micro-benchmark instead of the decode bench")
     ap.add_argument("--shapes", default="14336x4096,4096x4096,1024x4096,4096x14336")
     ap.add_argument("--batches", default="1,2,4,8")
