@@ -406,6 +406,34 @@ def run_kernels(args):
                       flush=True)
             del ws
             torch.cuda.empty_cache()
+    elif args.kernel == "prefill":   # many-row linears: bit-exact device dequant + cuBLAS vs the stock path
+        import torch.nn.functional as F
+        from b200kernels.linear4bit import dequantize_torch
+        M = args.prefill_rows
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+        for (N, K) in shapes:
+            w = (torch.randn(N, K, generator=torch.Generator().manual_seed(N + K)) * 0.02).half().to(dev)
+            packed, qs = quantize_nf4(w, nested=not args.plain)
+            p = torch.nn.Parameter(packed, requires_grad=False)
+            p.quant_state = qs
+            nf = NF4Weight(p)
+            del w
+            x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().to(dev)
+            wbuf = torch.empty(N, K, dtype=torch.half, device=dev)
+            y = torch.empty(M, N, dtype=torch.half, device=dev)
+            t_deq = _graph_time_us([lambda: nf.dequantize(out=wbuf)])
+            t_gemm = _graph_time_us([lambda: torch.matmul(x, wbuf.T, out=y)])
+            t_ours = _graph_time_us([lambda: (nf.dequantize(out=wbuf), torch.matmul(x, wbuf.T, out=y))])
+            t_stock = _graph_time_us([lambda: y.copy_(F.linear(x, dequantize_torch(p.data, qs, torch.half)))])
+            deq_bytes = nf.nbytes + N * K * 2
+            print(json.dumps({"kernel": "prefill_linear", "N": N, "K": K, "M": M, "nested": not args.plain,
+                              "dequant_us": round(t_deq, 2), "dequant_GBps": round(deq_bytes / t_deq / 1e3, 1),
+                              "dequant_pct_peak": round(100 * deq_bytes / t_deq / 1e3 / peak, 1),
+                              "gemm_only_us": round(t_gemm, 2), "ours_us": round(t_ours, 2),
+                              "stock_us": round(t_stock, 2), "dequant_tax_ours": round(t_ours / t_gemm - 1, 3),
+                              "dequant_tax_stock": round(t_stock / t_gemm - 1, 3), "peak_kind": peak_kind}), flush=True)
+            del nf, p, packed, qs, wbuf, y
+            torch.cuda.empty_cache()
     elif args.kernel == "lm_head":   # Mistral-7B head 32000x4096 fp16 + argmax (two weight copies > 2x L2)
         from b200kernels.lm_head import lm_head_argmax
         V, K = 32000, 4096
@@ -454,10 +482,11 @@ def run_kernels(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["nf4", "attention", "lm_head"], default=None,
+    ap.add_argument("--kernel", choices=["nf4", "attention", "lm_head", "prefill"], default=None,
                     help="kernel micro-benchmark instead of the decode bench")
     ap.add_argument("--shapes", default="14336x4096,4096x4096,1024x4096,4096x14336")
     ap.add_argument("--batches", default="1,2,4,8")
+    ap.add_argument("--prefill-rows", type=int, default=2048, help="rows (batch x prompt) for --kernel prefill")
     ap.add_argument("--contexts", default="128,512,2048,4096")
     ap.add_argument("--ragged", action="store_true")
     ap.add_argument("--plain", action="store_true", help="fp32 absmax instead of double quantisation")
