@@ -3,8 +3,10 @@
 The same split as transformers' Mistral ``base_model_tp_plan``: q/k/v/gate/up are split by output
 rows (column parallel), o/down by input columns (row parallel), KV heads ``KVH / world`` per rank with
 their ``H / KVH`` query heads kept together; after o_proj and after down_proj the partial hidden
-states are summed with an NCCL all-reduce. Embedding, norms and lm_head stay replicated. No
-counterpart in the reference (single GPU); this is the tensor-parallel mode it plans.
+states are summed across the ranks (fused into the GEMM epilogue, the one-shot peer kernel, or NCCL).
+The decode engine splits lm_head by vocabulary rows (``lm_head.merge_keys`` merges the ranks' argmax);
+embedding and norms stay replicated. No counterpart in the reference (single GPU); this is the
+tensor-parallel mode it plans.
 
 NF4 shards are cut from the bitsandbytes tensors without re-quantising: a column-parallel shard is a
 row range of packed bytes and per-block scales; a row-parallel shard is a column range of every row.
