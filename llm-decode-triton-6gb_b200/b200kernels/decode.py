@@ -326,6 +326,20 @@ class DecodeEngine:
         self.pos.fill_(context)
         self.ids.random_(0, self.model.config.vocab_size, generator=g)
 
+    def check_peers(self) -> None:
+        """Raise if a tensor-parallel peer wait of this rank has timed out since the engine was built.
+
+        The peer all-reduce kernels bound every wait and count a timeout in a device-side error word
+        instead of hanging; after one, the sums of later steps are not trustworthy (a wait that
+        timed out reads whatever the peer's slot held). ``generate`` and ``teacher_forced`` call this
+        at their end; a caller driving ``step`` itself should call it (one device read) before it
+        trusts the tokens. A no-op without tensor parallelism."""
+        if self.tp is not None:
+            n = self.tp.peer_errors()
+            if n:
+                raise RuntimeError(f"tensor-parallel rank {self.tp.rank}: {n} peer all-reduce wait(s) timed out; "
+                                   "the decoded tokens since then are invalid")
+
     def full_logits(self) -> torch.Tensor:
         """The last step's logits [B, vocab]. Under tensor parallelism with the vocabulary-parallel
         head, every rank holds its slice and this gathers them (a collective: all ranks call it)."""
@@ -350,6 +364,7 @@ class DecodeEngine:
             self.ids.copy_(tokens[:, t - 1])
             preds.append(self.step().clone())
             logits.append(self.full_logits().float())
+        self.check_peers()
         return torch.stack(preds, 1), torch.stack(logits, 1)
 
     @torch.inference_mode()
@@ -360,6 +375,7 @@ class DecodeEngine:
             self.capture()
         for _ in range(new_tokens - 1):
             out.append(self.step().clone())
+        self.check_peers()
         return torch.stack(out, dim=1)
 
 

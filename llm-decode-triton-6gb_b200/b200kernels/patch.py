@@ -27,19 +27,42 @@ from .decode_attention import decode_attention
 from .linear4bit import Linear4bit
 from .nf4_gemm import NF4Weight, calibrate as _calibrate
 
-STATS = {"attn_kernel": 0, "attn_fallback": 0}
+class _Stats(dict):
+    """Attention path counters with the reference's keys (``attn_triton``: decode steps served by the
+    fast kernel, ``attn_fallback``: calls handed to HF's SDPA). ``attn_kernel`` is accepted as another
+    name for ``attn_triton`` (reads, writes and ``update``)."""
+
+    _ALIAS = {"attn_kernel": "attn_triton"}
+
+    def __getitem__(self, k):
+        return super().__getitem__(self._ALIAS.get(k, k))
+
+    def __setitem__(self, k, v):
+        super().__setitem__(self._ALIAS.get(k, k), v)
+
+    def get(self, k, default=None):
+        return super().get(self._ALIAS.get(k, k), default)
+
+    def update(self, *args, **kw):
+        for k, v in dict(*args, **kw).items():
+            self[k] = v
+
+
+STATS = _Stats(attn_triton=0, attn_fallback=0)
 
 
 def _attention(module, query, key, value, attention_mask, scaling=None, **kwargs):
     if query.shape[2] == 1 and attention_mask is None and query.dtype == key.dtype:
-        STATS["attn_kernel"] += 1
+        STATS["attn_triton"] += 1
         return decode_attention(query, key, value, scaling), None
     STATS["attn_fallback"] += 1
     return sdpa_attention_forward(module, query, key, value, attention_mask, scaling=scaling, **kwargs)
 
 
 def patch_attention():
-    # Re-registering "sdpa" keeps transformers' sdpa mask creation (which returns None when no mask is needed).
+    # The hook takes over the "sdpa" name rather than registering a new one: models configured for
+    # SDPA keep building their masks the SDPA way, and that builder passes no mask at all when a decode
+    # step needs none, which is the condition the fast path above tests for.
     AttentionInterface.register("sdpa", _attention)
 
 

@@ -20,6 +20,9 @@
 // Workspace per (b, h, split): unnormalised O[D] (fp32) and (m, l) with m in the log2 domain.
 #include <cstdio>
 
+#include <atomic>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace b2d {
@@ -549,7 +552,10 @@ static constexpr size_t kGqaNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
 static __device__ __align__(256) uint8_t b2d_gqa_noalloc_scratch[kGqaNoAllocScratchBytes];
 
 namespace {
-void* g_noalloc_scratch_ptr[64] = {nullptr};   // device address of the array, per device
+// Device address of the array, per device: looked up once under a lock; later calls (from any host
+// thread) read it without locking.
+std::atomic<void*> g_noalloc_scratch_ptr[64];
+std::mutex g_noalloc_lookup_mutex;
 }
 
 extern "C" int b2d_gqa_decode_noalloc(const void* q, int64_t sq_b, int64_t sq_h, const void* k, int64_t sk_b,
@@ -592,16 +598,19 @@ extern "C" int b2d_gqa_decode_noalloc(const void* q, int64_t sq_b, int64_t sq_h,
     if (e != cudaSuccess) set_cuda_error(e);
     return B2D_ERR_DEVICE;
   }
-  if (!g_noalloc_scratch_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, b2d_gqa_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_cuda_error(e);
-      return B2D_ERR_DEVICE;
+  void* scratch = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!scratch) {
+    std::lock_guard<std::mutex> lock(g_noalloc_lookup_mutex);
+    scratch = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!scratch) {
+      e = cudaGetSymbolAddress(&scratch, b2d_gqa_noalloc_scratch);
+      if (e != cudaSuccess || scratch == nullptr) {
+        set_cuda_error(e);
+        return B2D_ERR_DEVICE;
+      }
+      g_noalloc_scratch_ptr[dev].store(scratch, std::memory_order_release);
     }
-    g_noalloc_scratch_ptr[dev] = p;
   }
   return b2d_gqa_decode(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
-                        nsplit, chunk, dtype, g_noalloc_scratch_ptr[dev], kGqaNoAllocScratchBytes, out, so_b, so_h,
-                        out_dtype, stream);
+                        nsplit, chunk, dtype, scratch, kGqaNoAllocScratchBytes, out, so_b, so_h, out_dtype, stream);
 }

@@ -45,10 +45,14 @@ struct LmArgs {
   int static_w;
 };
 
-// Orders floats as signed integers (negative values with their magnitude bits flipped).
+// Orders floats as signed integers (negative values with their magnitude bits flipped), with torch.argmax's
+// rules for the special values: -0 and +0 compare equal (both map to the key of +0, so the lower index
+// wins), and every NaN is larger than any number (the first NaN wins).
 __device__ __forceinline__ long long argmax_key(float v, int64_t index) {
   int32_t b = __float_as_int(v);
-  if (b < 0) b ^= 0x7FFFFFFF;
+  if (v != v) b = 0x7FFFFFFF;
+  else if (b == static_cast<int32_t>(0x80000000u)) b = 0;
+  else if (b < 0) b ^= 0x7FFFFFFF;
   return (static_cast<long long>(b) << 32) | static_cast<long long>(0xFFFFFFFFu - static_cast<uint32_t>(index));
 }
 

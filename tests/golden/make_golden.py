@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only) and Triton:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference-checkout
 
 * ``nf4_gemm_ref_*.npz`` -- outputs of the reference's own NF4 Triton kernel
   (``profiling/kernels/nf4_gemm.py:37-64``) executed by the Triton CPU interpreter
@@ -122,7 +122,9 @@ def attention_cases():
 
 
 if __name__ == "__main__":
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path to the reference checkout>")
+    ref_root = sys.argv[1]
     kern = _ref_kernel(ref_root)
     gemm_cases(kern)
     dequant_cases(kern)

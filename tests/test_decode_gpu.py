@@ -42,9 +42,9 @@ def test_patched_hf_matches_stock_small(small_model):
     patch.patch_attention()
     patch.patch_linear4bit(small_model, verbose=False)
     try:
-        patch.STATS.update(attn_kernel=0, attn_fallback=0)
+        patch.STATS.update(attn_triton=0, attn_fallback=0)
         ours, lo = dec.hf_greedy(small_model, ids, 24, return_logits=True)
-        assert patch.STATS["attn_kernel"] > 0
+        assert patch.STATS["attn_triton"] > 0 and patch.STATS["attn_kernel"] == patch.STATS["attn_triton"]
     finally:
         patch.unpatch_attention()
         patch.unpatch_linear4bit(small_model)
@@ -70,20 +70,41 @@ def _first_div(a, b):
     return [(r != s).nonzero()[0].item() if (r != s).any() else None for r, s in zip(a, b)]
 
 
+def near_tie_report(preds, stock, ol, sl):
+    """Every teacher-forced step where our argmax differs from the stock one, with the evidence that it is
+    a rounding near-tie: the stock logits' margin between the stock choice and ours, the largest logit
+    error of ours at that step (the measured error bound there), and whether ours is the stock runner-up.
+
+    preds [B, T-1] / ol [B, T-1, V]: our predictions and logits after consuming stock[:, :t]; stock [B, T]
+    and sl [B, T, V]: the stock tokens and logits (sl[:, t] predicts stock[:, t])."""
+    flips = []
+    for b, j in (preds != stock[:, 1:]).nonzero().tolist():
+        s, o = sl[b, j + 1], ol[b, j]
+        ours, theirs = int(preds[b, j]), int(stock[b, j + 1])
+        second = s.topk(2).values[1].item()
+        flips.append({"seq": b, "step": j + 1, "stock": theirs, "ours": ours,
+                      "stock_margin": (s[theirs] - s[ours]).item(),
+                      "step_err_max": (o - s).abs().max().item(),
+                      "ours_is_stock_runner_up": s[ours].item() >= second})
+    return flips
+
+
 def test_mistral7b_greedy_128_vs_stock():
     """Full Mistral-7B shape (NF4, double quant), 4 x 256-token prompts, 128 greedy tokens.
 
     A random-init model has nearly flat logits, so greedy decoding amplifies any rounding difference
-    at a near-tie. The test therefore measures three things:
-      * teacher-forced: both paths consume the stock tokens; our logit error must stay below 1% of
-        the stock logits' standard deviation in RMS and 10% at its maximum over every step and
-        vocabulary entry, and our argmax must agree with stock on >= 98% of the steps;
-      * free-running token identity against stock (reported);
-      * a control: the stock path itself with an fp32-accumulated matmul (the reference's config-1
-        formulation, ``x.float() @ W.float().T``) -- equally valid rounding -- free-running against
-        stock (reported). Our free-running mismatches may not exceed the control's by more than one
-        sequence.
-    """
+    at a near-tie. What is asserted:
+      * teacher-forced (both paths consume the stock tokens): our logit error stays below 1% of the
+        stock logits' standard deviation in RMS and 10% at its maximum over every step and vocabulary
+        entry, and our argmax agrees with stock on >= 98% of the steps;
+      * every teacher-forced step where the argmaxes differ is a near-tie: the stock margin between
+        its choice and ours is within twice the largest logit error we make at that step (the
+        measured bound there), and our choice is the stock runner-up;
+      * every free-running divergence starts at such a step: up to its first differing token a
+        sequence has consumed exactly the stock tokens, so its first divergence is one of the
+        teacher-forced flips above.
+    Reported: the flips with their margins, the free-running match, and a control (the stock path
+    itself with an fp32-accumulated matmul, ``x.float() @ W.float().T`` -- equally valid rounding)."""
     import json
     from b200kernels import linear4bit
 
@@ -99,6 +120,7 @@ def test_mistral7b_greedy_128_vs_stock():
     rel = (err.abs().max() / scale).item()
     rms = (err.pow(2).mean().sqrt() / scale).item()
     agree = (preds == stock[:, 1:]).float().mean().item()
+    flips = near_tie_report(preds, stock, ol, sl)
 
     orig = linear4bit.Linear4bit.forward
 
@@ -111,14 +133,19 @@ def test_mistral7b_greedy_128_vs_stock():
         ctl = dec.hf_greedy(model, ids, 128)
     finally:
         linear4bit.Linear4bit.forward = orig
+    first_div = _first_div(ours, stock)
     report = {"teacher_forced_max_logit_err_over_std": rel, "teacher_forced_rms_logit_err_over_std": rms,
-              "teacher_forced_argmax_agreement": agree,
-              "ours_vs_stock_match": (ours == stock).float().mean().item(), "ours_first_div": _first_div(ours, stock),
+              "teacher_forced_argmax_agreement": agree, "teacher_forced_flips": flips,
+              "ours_vs_stock_match": (ours == stock).float().mean().item(), "ours_first_div": first_div,
               "control_vs_stock_match": (ctl == stock).float().mean().item(),
               "control_first_div": _first_div(ctl, stock)}
     print("GREEDY_PARITY", json.dumps(report))
     assert rel < 0.1 and rms < 1e-2, report
     assert agree >= 0.98, report
-    n_ours = sum(d is not None for d in report["ours_first_div"])
-    n_ctl = sum(d is not None for d in report["control_first_div"])
-    assert n_ours <= n_ctl + 1, report
+    for f in flips:
+        assert f["stock_margin"] <= 2 * f["step_err_max"], f
+        assert f["ours_is_stock_runner_up"], f
+    flip_steps = {(f["seq"], f["step"]) for f in flips}
+    for b, d in enumerate(first_div):
+        if d is not None:
+            assert d >= 1 and (b, d) in flip_steps, (b, d, sorted(flip_steps))

@@ -12,8 +12,14 @@ from b200kernels.lm_head import merge_keys
 
 
 def key(value: float, index: int) -> int:
+    """The key ``b2d_lm_head_argmax`` forms (``argmax_key`` in csrc/lm_head.cu): -0 is folded onto +0 and
+    every NaN onto the largest key, as torch.argmax orders them."""
     b = struct.unpack("<i", struct.pack("<f", value))[0]
-    if b < 0:
+    if value != value:
+        b = 0x7FFFFFFF
+    elif b == -0x80000000:
+        b = 0
+    elif b < 0:
         b ^= 0x7FFFFFFF
     return (b << 32) | (0xFFFFFFFF - index)
 
@@ -40,3 +46,15 @@ def test_key_order_matches_float_order():
     ks = [key(v, 10) for v in vals]
     assert ks == sorted(ks)
     assert key(1.0, 3) > key(1.0, 4)
+
+
+def test_signed_zero_and_nan_follow_torch_argmax():
+    """torch.argmax treats -0 and +0 as equal (first index wins) and NaN as the maximum (first NaN wins)."""
+    cases = [[0.0, -0.0, 0.0], [-0.0, 0.0], [-1.0, -0.0, 0.0, -0.0], [1.0, float("nan"), 2.0, float("nan")],
+             [float("inf"), float("nan")], [float("-inf"), -0.0], [-2.0, float("-nan"), 5.0]]
+    for vals in cases:
+        t = torch.tensor(vals)
+        best = max(range(len(vals)), key=lambda i: key(vals[i], i))
+        assert best == torch.argmax(t).item(), vals
+        keys = torch.tensor([[key(v, i) for i, v in enumerate(vals)]]).T   # one shard per element
+        assert merge_keys(keys).item() == torch.argmax(t).item(), vals

@@ -53,6 +53,30 @@ def test_ties_take_the_first_index():
     assert torch.equal(ids, torch.argmax(logits, -1))
 
 
+def test_signed_zero_and_nan_follow_torch_argmax():
+    """Logits of -0 and +0 are equal maxima (the lower index wins) and a NaN logit is the maximum (the
+    first NaN wins), as torch.argmax decides. Every other row is strongly negative."""
+    M, V, K = 2, 64, 256
+    x = torch.zeros(M, K, dtype=torch.float16, device=DEV)
+    x[:, 0] = 0.25
+    x[:, 1] = 1.0
+    w = torch.zeros(V, K, dtype=torch.float16, device=DEV)
+    w[:, 1] = -4.0                                  # every row: logit -4 ...
+    w[5, 1] = 0.0
+    w[5, 0] = -(2.0 ** -24)                         # ... row 5: -2^-26, which rounds to -0 in fp16
+    w[9, 1] = 0.0                                   # ... row 9: exactly +0
+    logits, ids, _ = lm_head_argmax(x, w)
+    torch.cuda.synchronize()
+    assert logits[0, 5].item() == 0.0 and str(logits[0, 5].item()) == "-0.0" and str(logits[0, 9].item()) == "0.0"
+    assert ids.tolist() == [5, 5] and torch.equal(ids, torch.argmax(logits, -1))
+    w[12, 2] = float("nan")                         # rows 12 and 20 give NaN logits (NaN * 0 is NaN)
+    w[20, 3] = float("nan")
+    logits, ids, _ = lm_head_argmax(x, w)
+    torch.cuda.synchronize()
+    assert logits[:, 12].isnan().all() and logits[:, 20].isnan().all()
+    assert ids.tolist() == [12, 12] and torch.equal(ids, torch.argmax(logits, -1))
+
+
 def test_vocab_shards_merge_to_full_argmax():
     M, V, K, R = 8, 32000, 4096, 4
     x, w = make(M, V, K, torch.float16, 11)

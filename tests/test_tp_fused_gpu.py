@@ -1,7 +1,7 @@
 """GPU (one device): the tensor-parallel all-reduce fused into the NF4 GEMM epilogue
 (``b2d_nf4_gemm_multi`` mode B2D_SEG_ALLREDUCE) and its consumer ``b2d_allreduce_add_rmsnorm``.
 
-The ranks of a world of 1, 2 or 4 are emulated on one GPU: each rank's buffer is a plain device
+The ranks of a world of 1, 2, 4 or 8 are emulated on one GPU: each rank's buffer is a plain device
 allocation, every rank's GEMM pushes its partial product into all buffers, and only then (stream
 order, nothing in flight) does each rank's consumer run, so no kernel ever waits for another launch.
 Bar: bit-identical to the unfused sequence -- each rank's GEMM output rounded to fp16, summed over
@@ -64,7 +64,7 @@ def consume(ep, residual, weight_, eps, out, flags=0):
               flags, _lib.stream_ptr(residual.device))
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
 @pytest.mark.parametrize("M", [1, 3, 8])
 @pytest.mark.parametrize("nested", [True, False])
 def test_fused_allreduce_matches_unfused(world, M, nested):
