@@ -474,19 +474,23 @@ def run_b200(args):
 
     # ---- roofline: the model's gate_proj matmuls (this rank's 14336/N x 4096 NF4 shards) at batch B,
     # launched back to back from a CUDA graph on the bench stream and timed with events on that stream
-    # (no host gaps); consecutive launches read different weights, so every launch streams its
-    # weights from HBM.
+    # (no host gaps), each launched as the decode step launches its GEMMs (programmatic dependent launch
+    # with static weights: a launch's prologue overlaps the previous launch's tail); consecutive launches
+    # read different weights, so every launch streams its weights from HBM.
+    from b200kernels import _lib as L
+    from b200kernels.nf4_gemm import NF4Group
     x = torch.randn(B, 4096, generator=torch.Generator().manual_seed(3)).half().to(dev)
     gates = [wd["gate"] for wd in eng.w]
+    ggrps = [NF4Group([wgt]) for wgt in gates]
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(st):
-        ys = [wgt.matmul(x) for wgt in gates]
+        ys = [gr.matmul(x)[0] for gr in ggrps]
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=st):
-        for wgt, y in zip(gates, ys):
-            wgt.matmul(x, out=y)
+        for gr, y in zip(ggrps, ys):
+            gr.matmul(x, [y], flags=L.LAUNCH_PDL | L.STATIC_WEIGHTS)
     durs = []
     for _ in range(REPEATS):
         with torch.cuda.stream(st):
@@ -589,7 +593,8 @@ def run_b200(args):
                 "config": cfg,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
                         "d2h_bytes_per_step": B * 8, "wall_s": round(e2e_wall, 4)},
-                "roofline": {"bound": "hbm", "kernel": "nf4_gemm_pipe_kernel (gate_proj" + shard + ", nested)",
+                "roofline": {"bound": "hbm", "kernel": "nf4_gemm_pipe_kernel (gate_proj" + shard + ", nested, "
+                                                       "decode-step launch mode)",
                              "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                              "frac": round(achieved / peak, 4),
                              "traffic": traffic_from_profile() if world == 1 else None,
@@ -663,9 +668,17 @@ def run_kernels(args):
                         ws[0].matmul(x)
                     torch.cuda.synchronize()
                     continue
-                us = _graph_time_us([lambda w=w: w.matmul(x) for w in ws])
+                if args.pdl:   # as the decode step launches it: programmatic dependent launch, static weights
+                    from b200kernels import _lib as L
+                    from b200kernels.nf4_gemm import NF4Group
+                    grps = [NF4Group([w]) for w in ws]
+                    yo = torch.empty(M, N, dtype=x.dtype, device=dev)
+                    us = _graph_time_us([lambda gr=gr: gr.matmul(x, [yo], flags=L.LAUNCH_PDL | L.STATIC_WEIGHTS)
+                                         for gr in grps])
+                else:
+                    us = _graph_time_us([lambda w=w: w.matmul(x) for w in ws])
                 nbytes = ws[0].nbytes + x.numel() * 2 + M * N * 2
-                print(json.dumps({"kernel": "nf4_gemm", "N": N, "K": K, "M": M, "nested": not args.plain,
+                print(json.dumps({"kernel": "nf4_gemm", "N": N, "K": K, "M": M, "nested": not args.plain, "pdl": args.pdl,
                                   "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
                                   "pct_peak": round(100 * nbytes / us / 1e3 / peak, 1), "peak_kind": peak_kind}),
                       flush=True)
@@ -756,6 +769,9 @@ def main():
     ap.add_argument("--ragged", action="store_true")
     ap.add_argument("--plain", action="store_true", help="fp32 absmax instead of double quantisation")
     ap.add_argument("--profile-iters", type=int, default=0)
+    ap.add_argument("--pdl", action="store_true",
+                    help="nf4 micro-benchmark: launch as the decode step does (programmatic dependent launch, "
+                         "static weights)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)

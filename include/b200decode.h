@@ -274,7 +274,7 @@ int b2d_silu_mul(const void* gate, int64_t ldg, const void* up, int64_t ldu, voi
  * largest logit of row m, ties to the lowest index -- replaces the reference decode step's
  * `lm_head` GEMV followed by `logits.argmax(-1)` (profiling/common.py decode_step; the stock
  * LlamaForCausalLM/MistralForCausalLM head) with one launch. W is the [V, K] row-major head weight
- * (row stride ldw), x [M, K]; 1 <= M <= 8, K % 256 == 0, 16-byte aligned x and W, ldx/ldw % 8 == 0.
+ * (row stride ldw), x [M, K]; 1 <= M <= 64, K % 256 == 0, 16-byte aligned x and W, ldx/ldw % 8 == 0.
  * Outputs (any may be NULL, not all): logits [M, V] (row stride ld_logits), ids int64 [M], keys [M] =
  * the packed (value, index) maxima, ordered as signed 64-bit integers -- for a vocabulary-parallel
  * shard, indices are offset by vocab_offset and the shards' results merge by taking the maximum key

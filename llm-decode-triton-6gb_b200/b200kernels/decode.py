@@ -12,7 +12,7 @@ with per-sequence lengths and captures one whole decode step (32 layers) in a CU
 * the glue ops (residual add + RMSNorm, rotary embedding + KV append) -> this library's kernels
   (``fused=True``), every launch a programmatic dependent of the previous one; or the HF modules
   themselves (``fused=False``);
-* lm_head + argmax -> one ``lm_head_argmax`` launch at batch <= 8 (fused mode; vocabulary-parallel
+* lm_head + argmax -> one ``lm_head_argmax`` launch at batch <= 64 (fused mode; vocabulary-parallel
   under tensor parallelism, the shards' maxima merged by one all-gather of 8-byte keys); otherwise
   torch ops. The embedding stays a torch op.
 

@@ -13,7 +13,7 @@ import torch
 
 from . import _lib
 
-MAX_M = 8
+MAX_M = 64
 _WS: dict = {}
 
 
@@ -31,7 +31,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, logits: torch.Tensor | None = None,
                    ids: torch.Tensor | None = None, keys: torch.Tensor | None = None, vocab_offset: int = 0,
                    flags: int = 0):
-    """x [M, K] (M <= 8), weight [V, K] -> (logits [M, V] or None, ids int64 [M] or None, keys or None).
+    """x [M, K] (M <= 64), weight [V, K] -> (logits [M, V] or None, ids int64 [M] or None, keys or None).
 
     Pass preallocated outputs to reuse them (CUDA-graph capture); with none given, logits and ids are
     allocated."""

@@ -29,6 +29,17 @@ from . import _lib
 _WS: dict = {}
 
 
+ERR_WORD_OFFSET = 65536 - 64   # workspace byte offset of the TMA-staged kernel's timeout counter
+
+
+def gemm_errors(device: torch.device) -> int:
+    """Timed-out pipeline waits recorded by the TMA-staged NF4 kernel in this stream's workspace (0 when
+    healthy; a nonzero count means some launch computed from incomplete weight tiles)."""
+    stream = torch.cuda.current_stream(device)
+    ws = _WS.get((device.index, stream.cuda_stream))
+    return 0 if ws is None else int(ws[ERR_WORD_OFFSET:ERR_WORD_OFFSET + 4].view(torch.int32).item())
+
+
 def gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Zero-initialised scratch for ``b2d_nf4_gemm``, one per (device, stream). The kernel leaves
     its counters at zero, so the buffer is reused across calls on the same stream."""
@@ -193,11 +204,15 @@ class NF4Group:
         import ctypes
         self._code_host = (ctypes.c_float * 16)(*w0.code.float().cpu().tolist())   # codebook passed by value
         self._segs = (_lib.Nf4Segment * len(weights))()
+        # segments whose double-quant tables hold the same values share one table (the TMA-staged kernel
+        # keeps a single table per launch)
+        same_code2 = w0.nested and all(torch.equal(w.code2, w0.code2) for w in weights)
         for i, w in enumerate(weights):
             sg = self._segs[i]
             sg.packed, sg.ld_packed = _lib.ptr(w.packed), w.ld_packed
             sg.absmax, sg.ld_absmax = _lib.ptr(w.absmax), w.ld_absmax
-            sg.code2, sg.absmax2, sg.offset = _lib.ptr(w.code2), _lib.ptr(w.absmax2), w.offset
+            sg.code2 = _lib.ptr(w0.code2 if same_code2 else w.code2)
+            sg.absmax2, sg.offset = _lib.ptr(w.absmax2), w.offset
             sg.gblk_base, sg.gblk_row_stride = w.gblk_base, w.gblk_row_stride
             sg.code, sg.N = _lib.ptr(w.code), w.N
 

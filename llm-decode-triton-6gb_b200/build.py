@@ -18,7 +18,7 @@ REPO_ROOT = PKG_ROOT.parent
 CSRC = PKG_ROOT / "csrc"
 INCLUDE = REPO_ROOT / "include"
 LIB_PATH = PKG_ROOT / "b200kernels" / "libb200decode.so"
-SOURCES = ["capi.cu", "nf4_gemm.cu", "nf4_format.cu", "gqa_decode.cu", "decode_glue.cu", "tp_allreduce.cu", "lm_head.cu"]
+SOURCES = ["capi.cu", "nf4_gemm.cu", "nf4_gemm_tma.cu", "nf4_format.cu", "gqa_decode.cu", "decode_glue.cu", "tp_allreduce.cu", "lm_head.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,5 +1,5 @@
 // lm_head GEMV + greedy argmax for decode (sm_100a): logits[M, V] = x[M, K] @ W[V, K]^T in fp16/bf16 with
-// fp32 accumulation, and the index of each row's largest logit, in one launch.
+// fp32 accumulation, and the index of each row's largest logit, in one launch (M <= 64 tokens).
 //
 // The reference's decode step runs `lm_head` as a cuBLAS GEMV followed by a separate `argmax`
 // (profiling/common.py decode_step: model forward -> logits[:, -1].argmax(-1)); the weight (V x K fp16,
@@ -7,7 +7,8 @@
 //  * CTA = 8 warps on a tile of 16 vocabulary rows; the warps split K (K/8 each) and every warp
 //    streams its slice of the 16 rows with 16-byte loads straight into mma.sync A fragments (the
 //    reduction axis is permuted per lane, identically for W and x, so each lane's 8 weights and 8
-//    activations per 32-wide chunk are contiguous), 8 chunks in flight per lane;
+//    activations per 32-wide chunk are contiguous), 8 chunks in flight per lane (4 from 17 tokens up);
+//    each A fragment feeds one MMA per 8 tokens, so the weight is read once for any batch <= 64;
 //  * the 8 warps' partial sums are added in warp order in shared memory, rounded once to the model
 //    dtype (the logits torch would hold), and each row's value enters a per-token argmax key
 //    (ordered value << 32 | ~index): the largest value wins, ties go to the lowest index, which is
@@ -27,8 +28,7 @@ namespace {
 constexpr int kLmWarps = 8;
 constexpr int kLmThreads = kLmWarps * 32;
 constexpr int kLmRows = 16;     // vocabulary rows per tile (one m16 MMA tile)
-constexpr int kLmUnroll = 8;    // 32-wide K chunks in flight per lane
-constexpr int kLmMaxM = 8;
+constexpr int kLmMaxM = 64;     // tokens per launch (eight n8 MMA tiles)
 constexpr size_t kLmCounterBytes = 256;
 
 struct LmArgs {
@@ -65,18 +65,27 @@ __device__ __forceinline__ uint4 ld_x_u4(const void* p) {
   return v;
 }
 
-template <typename T>
+// NT = n8 token tiles (M <= 8 NT); UNROLL = 32-wide K chunks in flight per lane.
+template <typename T, int NT, int UNROLL>
 __global__ void __launch_bounds__(kLmThreads, 2) lm_head_argmax_kernel(const LmArgs a) {
   pdl_launch_dependents();
-  __shared__ float red[kLmWarps][kLmRows][kLmMaxM];
-  __shared__ long long s_key[4][kLmMaxM];
+  constexpr int TOK = 8 * NT;                                      // token columns
+  constexpr int RPT = kLmRows * TOK >= kLmThreads ? kLmRows * TOK / kLmThreads : 1;   // rows per thread
+  constexpr int GROUPS = TOK < 32 ? kLmWarps : kLmThreads / TOK;   // partial maxima per token
+  __shared__ float red[kLmWarps][kLmRows][TOK];
+  __shared__ long long s_part[GROUPS][TOK];
   __shared__ int s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
   const int kw = a.K / kLmWarps;                 // this warp's K slice
   const int k0 = warp * kw + tq * 8;
   const int nchunks = kw / 32;
   const T* x = static_cast<const T*>(a.x);
-  const T* xr = x + static_cast<int64_t>(g < a.M ? g : a.M - 1) * a.ldx + k0;   // clamped: columns >= M unused
+  const T* xr[NT];                               // token nt*8 + g (clamped: columns >= M unused)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = nt * 8 + g;
+    xr[nt] = x + static_cast<int64_t>(tok < a.M ? tok : a.M - 1) * a.ldx + k0;
+  }
   long long best = LLONG_MIN;                    // threads tid < M: this CTA's best key of token tid
   bool waited = false;
   if (!a.static_w) { pdl_wait(); waited = true; }
@@ -84,11 +93,13 @@ __global__ void __launch_bounds__(kLmThreads, 2) lm_head_argmax_kernel(const LmA
     const int r0 = tile * kLmRows + g, r1 = r0 + 8;
     const T* wa = static_cast<const T*>(a.w) + static_cast<int64_t>(r0 < a.V ? r0 : a.V - 1) * a.ldw + k0;
     const T* wb = static_cast<const T*>(a.w) + static_cast<int64_t>(r1 < a.V ? r1 : a.V - 1) * a.ldw + k0;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int ch = 0; ch < nchunks; ch += kLmUnroll) {
-      uint4 va[kLmUnroll], vb[kLmUnroll];
+    float c[NT][4];
 #pragma unroll
-      for (int u = 0; u < kLmUnroll; ++u) {
+    for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
+    for (int ch = 0; ch < nchunks; ch += UNROLL) {
+      uint4 va[UNROLL], vb[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
         if (ch + u < nchunks) {
           va[u] = ldg_stream_u4(wa + (ch + u) * 32);
           vb[u] = ldg_stream_u4(wb + (ch + u) * 32);
@@ -96,49 +107,70 @@ __global__ void __launch_bounds__(kLmThreads, 2) lm_head_argmax_kernel(const LmA
       }
       if (!waited) { pdl_wait(); waited = true; }   // x is the previous kernel's output
 #pragma unroll
-      for (int u = 0; u < kLmUnroll; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         if (ch + u < nchunks) {
-          const uint4 vx = ld_x_u4(xr + (ch + u) * 32);   // x slice: L1-resident after the first tile
-          Mma<T>::run(c, va[u].x, vb[u].x, va[u].y, vb[u].y, vx.x, vx.y);
-          Mma<T>::run(c, va[u].z, vb[u].z, va[u].w, vb[u].w, vx.z, vx.w);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint4 vx = ld_x_u4(xr[nt] + (ch + u) * 32);   // x slice: L1-resident after the first tile
+            Mma<T>::run(c[nt], va[u].x, vb[u].x, va[u].y, vb[u].y, vx.x, vx.y);
+            Mma<T>::run(c[nt], va[u].z, vb[u].z, va[u].w, vb[u].w, vx.z, vx.w);
+          }
         }
       }
     }
-    // C fragment: c0, c1 = row g, tokens 2tq, 2tq+1; c2, c3 = row g + 8
-    red[warp][g][2 * tq] = c[0];
-    red[warp][g][2 * tq + 1] = c[1];
-    red[warp][g + 8][2 * tq] = c[2];
-    red[warp][g + 8][2 * tq + 1] = c[3];
+    // C fragment of token tile nt: c0, c1 = row g, tokens 8nt + 2tq, +1; c2, c3 = row g + 8
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      red[warp][g][8 * nt + 2 * tq] = c[nt][0];
+      red[warp][g][8 * nt + 2 * tq + 1] = c[nt][1];
+      red[warp][g + 8][8 * nt + 2 * tq] = c[nt][2];
+      red[warp][g + 8][8 * nt + 2 * tq + 1] = c[nt][3];
+    }
     __syncthreads();
-    if (tid < kLmRows * kLmMaxM) {
-      const int row = tid >> 3, tok = tid & 7;
-      float s = 0.f;
-#pragma unroll
-      for (int w = 0; w < kLmWarps; ++w) s += red[w][row][tok];
-      const int64_t vr = static_cast<int64_t>(tile) * kLmRows + row;
-      const T h = Dt<T>::from_f32(s);
+    // thread (row group rg, token tok): RPT rows of the tile for one token; the warps' partials are added in
+    // warp order and rounded once to the model dtype (the logits torch would hold), and the thread keeps
+    // the largest argmax key of its rows
+    {
+      const int tok = tid % TOK, rg = tid / TOK;
       long long key = LLONG_MIN;
-      if (vr < a.V && tok < a.M) {
-        if (a.logits) static_cast<T*>(a.logits)[tok * a.ldl + vr] = h;
-        key = argmax_key(Dt<T>::to_f32(h), a.vocab_offset + vr);
-      }
-      // max over the 4 rows of this warp (lanes tok, tok+8, tok+16, tok+24), then over the 4 warps
+      if (rg * RPT < kLmRows) {
 #pragma unroll
-      for (int o = 8; o < 32; o <<= 1) {
+        for (int i = 0; i < RPT; ++i) {
+          const int row = rg * RPT + i;
+          float s = 0.f;
+#pragma unroll
+          for (int w = 0; w < kLmWarps; ++w) s += red[w][row][tok];
+          const int64_t vr = static_cast<int64_t>(tile) * kLmRows + row;
+          const T h = Dt<T>::from_f32(s);
+          if (vr < a.V && tok < a.M) {
+            if (a.logits) static_cast<T*>(a.logits)[tok * a.ldl + vr] = h;
+            const long long k = argmax_key(Dt<T>::to_f32(h), a.vocab_offset + vr);
+            key = k > key ? k : key;
+          }
+        }
+      }
+      // row groups sharing a warp reduce through shuffles first (lane = local row group * TOK + tok)
+#pragma unroll
+      for (int o = TOK; o < 32; o <<= 1) {
         const long long other = __shfl_xor_sync(0xffffffffu, key, o);
         key = other > key ? other : key;
       }
-      if (lane < kLmMaxM) s_key[warp][lane] = key;
+      if (TOK < 32) {
+        if (lane < TOK) s_part[warp][tok] = key;
+      } else {
+        s_part[rg][tok] = key;
+      }
     }
     __syncthreads();
-    if (tid < kLmMaxM) {
+    if (tid < TOK) {
 #pragma unroll
-      for (int w = 0; w < 4; ++w) best = s_key[w][tid] > best ? s_key[w][tid] : best;
+      for (int w = 0; w < GROUPS; ++w) best = s_part[w][tid] > best ? s_part[w][tid] : best;
     }
+    __syncthreads();   // red / s_part are rewritten by the next tile
   }
   if (!waited) pdl_wait();
   // publish this CTA's best keys; the last CTA merges every slot in CTA order
-  if (tid < kLmMaxM) {
+  if (tid < TOK) {
     a.slots[blockIdx.x * kLmMaxM + tid] = best;
     __threadfence();
   }
@@ -160,6 +192,14 @@ __global__ void __launch_bounds__(kLmThreads, 2) lm_head_argmax_kernel(const LmA
 }
 
 int lm_grid(int tiles, int sm_count) { return tiles < 2 * sm_count ? tiles : 2 * sm_count; }
+
+template <typename T>
+int launch_lm(const LmArgs& a, int grid, cudaStream_t s, bool pdl) {
+  if (a.M <= 8) return launch_kernel(lm_head_argmax_kernel<T, 1, 8>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
+  if (a.M <= 16) return launch_kernel(lm_head_argmax_kernel<T, 2, 8>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
+  if (a.M <= 32) return launch_kernel(lm_head_argmax_kernel<T, 4, 4>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
+  return launch_kernel(lm_head_argmax_kernel<T, 8, 4>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
+}
 
 }  // namespace
 }  // namespace b2d
@@ -200,6 +240,6 @@ extern "C" int b2d_lm_head_argmax(const void* x, int64_t ldx, const void* w, int
   const int grid = lm_grid(a.tiles, di.sm_count);
   const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == B2D_F16) return launch_kernel(lm_head_argmax_kernel<__half>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
-  return launch_kernel(lm_head_argmax_kernel<__nv_bfloat16>, dim3(grid), dim3(kLmThreads), 0, s, pdl, a);
+  if (dtype == B2D_F16) return launch_lm<__half>(a, grid, s, pdl);
+  return launch_lm<__nv_bfloat16>(a, grid, s, pdl);
 }

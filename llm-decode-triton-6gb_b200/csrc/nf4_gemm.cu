@@ -25,9 +25,12 @@
 //  * The MMA reduction dimension is permuted so that each thread's 8 bytes of a block row are
 //    contiguous in memory and the matching 16 activations are contiguous too:
 //    thread (g, t) at k-step s owns bytes 8t+2s, 8t+2s+1 of its block row = k offsets 16t+4s+{0..3}.
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
+#include "nf4_tma.cuh"
 
 namespace b2d {
 
@@ -969,7 +972,28 @@ __global__ void __launch_bounds__(kSimtThreads) nf4_gemv_simt_kernel(const GemmA
 // Workspace layout: a fixed-size counter region first (so calls of any shape agree on where the
 // counters live and always find them zero), then the per-CTA partial slots.
 constexpr size_t kCounterBytes = 64 * 1024;
-constexpr int64_t kMaxGroups = kCounterBytes / 4;
+constexpr size_t kErrWordOffset = kCounterBytes - 64;   // the TMA-staged kernel's timeout counter
+constexpr int64_t kMaxGroups = kErrWordOffset / 4;
+
+// Which M <= 8 kernel serves a launch: the register-staged one (default: measured faster on B200, in
+// isolation and inside the decode step), or, with B2D_NF4_KERNEL=tma in the environment, the TMA-staged
+// one when its rules are met (read at every call: a comparison can switch between calls).
+bool tma_path_enabled() {
+  const char* v = std::getenv("B2D_NF4_KERNEL");
+  return v && std::strcmp(v, "tma") == 0;
+}
+
+Nf4TmaSegment tma_segment(const uint8_t* packed, int64_t ld_packed, const void* absmax, int64_t ld_absmax,
+                          const float* code2, const float* absmax2, float offset, int64_t gblk_base,
+                          int64_t gblk_row_stride, int N, void* y, int64_t ldy) {
+  Nf4TmaSegment t;
+  t.packed = packed; t.ld_packed = ld_packed;
+  t.absmax = absmax; t.ld_absmax = ld_absmax;
+  t.code2 = code2; t.absmax2 = absmax2; t.offset = offset;
+  t.gblk_base = gblk_base; t.gblk_row_stride = gblk_row_stride;
+  t.N = N; t.y = y; t.ldy = ldy;
+  return t;
+}
 
 struct GemmConfig {
   int rt, nt, cb, nw;
@@ -1181,6 +1205,19 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   if ((st = choose_config(M, N, K, c4, di, &c)) != B2D_OK) return st;
   if (!workspace || workspace_bytes < c.counter_bytes + c.partial_bytes) return B2D_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return B2D_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 8 && tma_path_enabled()) {
+    Nf4TmaLaunch L;
+    std::memset(&L, 0, sizeof(L));
+    L.x = x; L.ldx = ldx; L.M = M; L.K = K; L.dtype = dtype; L.y_dtype = y_dtype; L.nested = nested;
+    L.mode = kTmaIndependent; L.nseg = 1;
+    L.seg[0] = tma_segment(packed, ld_packed, absmax, ld_absmax, code2, absmax2, offset, gblk_base, gblk_row_stride,
+                           N, y, ldy);
+    L.code_dev = code;
+    L.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kErrWordOffset);
+    const int r = nf4_tma_gemm(L, s);
+    if (r != kTmaNotApplicable) return r;
+  }
   GemmArgs a{};
   a.x = x; a.ldx = ldx;
   a.w = Nf4View{packed, ld_packed, absmax, ld_absmax, code2, absmax2, offset, gblk_base, gblk_row_stride, code};
@@ -1196,7 +1233,6 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
   a.static_w = 0;
   a.seg_end[0] = a.groups;
   a.seg[0] = SegView{a.w, y, ldy};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == B2D_F16)
     return y_dtype == B2D_F32 ? dispatch_tc<__half, float>(a, c, nested, s) : dispatch_tc<__half, __half>(a, c, nested, s);
   return y_dtype == B2D_F32 ? dispatch_tc<__nv_bfloat16, float>(a, c, nested, s)
@@ -1289,6 +1325,37 @@ extern "C" int b2d_nf4_gemm_multi(const void* x, int64_t ldx, const b2d_nf4_segm
   DeviceInfo di;
   int st;
   if ((st = device_info(&di)) != B2D_OK) return st;
+  if (!workspace || workspace_bytes < kCounterBytes) return B2D_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return B2D_ERR_ALIGN;
+  if (tma_path_enabled()) {
+    Nf4TmaLaunch L;
+    std::memset(&L, 0, sizeof(L));
+    L.x = x; L.ldx = ldx; L.M = M; L.K = K; L.dtype = dtype; L.y_dtype = y_dtype; L.nested = nested;
+    L.mode = pair ? kTmaSiluMul : (ar ? kTmaAllReduce : kTmaIndependent);
+    L.nseg = nseg;
+    for (int i = 0; i < nseg; ++i) {
+      const b2d_nf4_segment& sg = segs[i];
+      L.seg[i] = tma_segment(sg.packed, sg.ld_packed, sg.absmax, sg.ld_absmax, sg.code2, sg.absmax2, sg.offset,
+                             sg.gblk_base, sg.gblk_row_stride, sg.N, pair ? segs[0].y : sg.y,
+                             pair ? segs[0].ldy : sg.ldy);
+    }
+    L.code_dev = segs[0].code;
+    L.code_host = code_host;
+    L.pdl = (flags & B2D_LAUNCH_PDL) != 0;
+    L.static_w = (flags & B2D_STATIC_WEIGHTS) != 0;
+    if (ar) {
+      for (int p = 0; p < are->world; ++p) L.ar.peer[p] = static_cast<uint8_t*>(are->peer_bufs[p]);
+      L.ar.rank = are->rank;
+      L.ar.world = are->world;
+      L.ar.words = are->n_max / 2;
+      L.ar.step = are->step;
+      L.ar.site = are->site;
+      L.ar.sites = are->sites;
+    }
+    L.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kErrWordOffset);
+    const int r = nf4_tma_gemm(L, static_cast<cudaStream_t>(stream));
+    if (r != kTmaNotApplicable) return r;
+  }
   GemmConfig c;
   if (n_total > (int64_t(1) << 30)) return B2D_ERR_SHAPE;
   if ((st = choose_config(M, static_cast<int>(n_total), K, true, di, &c)) != B2D_OK) return st;

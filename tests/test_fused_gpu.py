@@ -33,6 +33,16 @@ def weight(N, K, nested, seed, dtype=torch.float16):
     return NF4Weight(p)
 
 
+@pytest.fixture(params=["register", "tma"])
+def nf4_kernel(request, monkeypatch):
+    """Runs a test once per M <= 8 NF4 kernel: the register-staged default and the TMA-staged one."""
+    if request.param == "tma":
+        monkeypatch.setenv("B2D_NF4_KERNEL", "tma")
+    else:
+        monkeypatch.delenv("B2D_NF4_KERNEL", raising=False)
+    return request.param
+
+
 def ulps(a: torch.Tensor, b: torch.Tensor) -> int:
     """Largest distance in units in the last place between two fp16/bf16 tensors of the same sign pattern."""
     ia = a.contiguous().view(torch.int16).to(torch.int32)
@@ -46,7 +56,7 @@ def ulps(a: torch.Tensor, b: torch.Tensor) -> int:
 @pytest.mark.parametrize("nested", [True, False])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("M", [1, 3, 8])
-def test_segmented_gemm_qkv(nested, dtype, M):
+def test_segmented_gemm_qkv(nested, dtype, M, nf4_kernel):
     K = 1024
     ws = [weight(512, K, nested, 1, dtype), weight(128, K, nested, 2, dtype), weight(96, K, nested, 3, dtype)]
     grp = NF4Group(ws)
@@ -64,7 +74,7 @@ def test_segmented_gemm_qkv(nested, dtype, M):
 
 @pytest.mark.parametrize("nested", [True, False])
 @pytest.mark.parametrize("M", [1, 8])
-def test_segmented_gemm_mistral_qkv_and_single(nested, M):
+def test_segmented_gemm_mistral_qkv_and_single(nested, M, nf4_kernel):
     K = 4096
     ws = [weight(4096, K, nested, 4), weight(1024, K, nested, 5), weight(1024, K, nested, 6)]
     x = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).half().to(DEV)
@@ -78,7 +88,7 @@ def test_segmented_gemm_mistral_qkv_and_single(nested, M):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("M", [1, 5, 8])
-def test_segmented_gemm_swiglu_epilogue(dtype, M):
+def test_segmented_gemm_swiglu_epilogue(dtype, M, nf4_kernel):
     K, N = 2048, 1536
     wg, wu = weight(N, K, True, 11, dtype), weight(N, K, True, 12, dtype)
     x = torch.randn(M, K, generator=torch.Generator().manual_seed(13)).to(dtype).to(DEV)

@@ -31,7 +31,8 @@ def check_logits(logits, x, w, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("M,V,K", [(1, 1000, 256), (3, 4099, 512), (8, 32000, 4096), (5, 17, 1024)])
+@pytest.mark.parametrize("M,V,K", [(1, 1000, 256), (3, 4099, 512), (8, 32000, 4096), (5, 17, 1024), (9, 3001, 512),
+                                   (16, 32000, 4096), (27, 777, 1024), (64, 32000, 4096)])
 def test_logits_and_argmax(dtype, M, V, K):
     x, w = make(M, V, K, dtype, M * 7 + V)
     for flags in (0, _lib.LAUNCH_PDL | _lib.STATIC_WEIGHTS):
@@ -77,8 +78,9 @@ def test_signed_zero_and_nan_follow_torch_argmax():
     assert ids.tolist() == [12, 12] and torch.equal(ids, torch.argmax(logits, -1))
 
 
-def test_vocab_shards_merge_to_full_argmax():
-    M, V, K, R = 8, 32000, 4096, 4
+@pytest.mark.parametrize("M", [8, 64])
+def test_vocab_shards_merge_to_full_argmax(M):
+    V, K, R = 32000, 4096, 4
     x, w = make(M, V, K, torch.float16, 11)
     full_logits, full_ids, _ = lm_head_argmax(x, w)
     keys = torch.empty(R, M, dtype=torch.int64, device=DEV)
@@ -106,9 +108,9 @@ def test_matches_stock_linear_argmax_up_to_near_ties():
 
 
 def test_rejects_unsupported_arguments():
-    x, w = make(9, 64, 256, torch.float16, 1)
+    x, w = make(65, 64, 256, torch.float16, 1)
     with pytest.raises(_lib.B2DError):
-        lm_head_argmax(x, w)                       # more than 8 rows
+        lm_head_argmax(x, w)                       # more than 64 rows
     x, w = make(2, 64, 320, torch.float16, 1)
     with pytest.raises(_lib.B2DError):
         lm_head_argmax(x, w)                       # K not a multiple of 256

@@ -36,7 +36,8 @@ def test_genuine_near_tie_passes():
     ol[b, j, top2.indices[1]] += 5e-4                                  # ours prefers it (error 5e-4)
     preds = ol.argmax(-1)
     (f,) = near_tie_report(preds, stock, ol, sl)
-    assert f["ours_is_stock_runner_up"] and f["stock_margin"] <= 2 * f["step_err_max"]
+    assert f["ours_is_stock_runner_up"] and f["ours_stock_rank"] == 2
+    assert f["stock_margin"] <= 2 * f["step_err_max"]
 
 
 def test_planted_non_tie_flips_are_flagged():
@@ -46,7 +47,7 @@ def test_planted_non_tie_flips_are_flagged():
     third = s.topk(3).indices[2]
     preds[b, j] = third                        # ours picks the stock third choice ...
     (f,) = near_tie_report(preds, stock, ol, sl)
-    assert not f["ours_is_stock_runner_up"]
+    assert not f["ours_is_stock_runner_up"] and f["ours_stock_rank"] == 3
     assert f["stock_margin"] > 2 * f["step_err_max"]   # ... with a margin far above our 1e-3 errors
 
 

@@ -64,10 +64,13 @@ def consume(ep, residual, weight_, eps, out, flags=0):
               flags, _lib.stream_ptr(residual.device))
 
 
+@pytest.mark.parametrize("kernel", ["register", "tma"])
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 @pytest.mark.parametrize("M", [1, 3, 8])
 @pytest.mark.parametrize("nested", [True, False])
-def test_fused_allreduce_matches_unfused(world, M, nested):
+def test_fused_allreduce_matches_unfused(world, M, nested, kernel, monkeypatch):
+    if kernel == "tma":   # both the pushing GEMM and the unfused comparison run the TMA-staged kernel
+        monkeypatch.setenv("B2D_NF4_KERNEL", "tma")
     N, Kr, sites, eps = 1024, 512, 2, 1e-5
     ws = {(r, s): weight(N, Kr, nested, 100 * s + r) for r in range(world) for s in range(sites)}
     groups = {k: NF4Group([w], mode="allreduce") for k, w in ws.items()}
