@@ -30,6 +30,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "nf4_tc5.cuh"
 #include "nf4_tma.cuh"
 
 namespace b2d {
@@ -983,6 +984,13 @@ bool tma_path_enabled() {
   return v && std::strcmp(v, "tma") == 0;
 }
 
+// 9..64 tokens run the tcgen05 kernel (nf4_tc5.cu) when its rules are met; B2D_NF4_TC5=0 in the
+// environment selects the register-staged mma.sync kernel instead (read at every call, for comparisons).
+bool tc5_path_enabled() {
+  const char* v = std::getenv("B2D_NF4_TC5");
+  return !(v && std::strcmp(v, "0") == 0);
+}
+
 Nf4TmaSegment tma_segment(const uint8_t* packed, int64_t ld_packed, const void* absmax, int64_t ld_absmax,
                           const float* code2, const float* absmax2, float offset, int64_t gblk_base,
                           int64_t gblk_row_stride, int N, void* y, int64_t ldy) {
@@ -1217,6 +1225,19 @@ extern "C" int b2d_nf4_gemm(const void* x, int64_t ldx, const uint8_t* packed, i
     L.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kErrWordOffset);
     const int r = nf4_tma_gemm(L, s);
     if (r != kTmaNotApplicable) return r;
+  }
+  if (M > 8 && tc5_path_enabled()) {
+    Nf4Tc5Launch L;
+    std::memset(&L, 0, sizeof(L));
+    L.x = x; L.ldx = ldx; L.M = M; L.K = K; L.dtype = dtype; L.y_dtype = y_dtype; L.nested = nested;
+    L.nseg = 1;
+    L.seg[0] = Nf4Tc5Segment{packed, ld_packed, absmax, ld_absmax, absmax2, offset, gblk_base, gblk_row_stride,
+                             N, y, ldy};
+    L.code_dev = code;
+    L.code2 = code2;
+    L.err = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kErrWordOffset);
+    const int r = nf4_tc5_gemm(L, s);
+    if (r != kTc5NotApplicable) return r;
   }
   GemmArgs a{};
   a.x = x; a.ldx = ldx;

@@ -294,3 +294,36 @@ def test_gemm_rejects_bad_arguments():
         nf.matmul(torch.randn(65, 256, device=DEV).half())       # M > 64
     with pytest.raises(_lib.B2DError):
         nf.matmul(torch.randn(2, 256, device=DEV))               # fp32 activations
+
+
+@pytest.mark.parametrize("N,K,M,nested,dtype", [(14336, 4096, 64, True, torch.float16),
+                                                (4096, 14336, 64, True, torch.float16),
+                                                (6144, 4096, 33, True, torch.float16),
+                                                (1040, 4096, 16, False, torch.float16),
+                                                (4096, 4096, 48, True, torch.bfloat16),
+                                                (1024, 1024, 9, True, torch.float16),
+                                                (64, 256, 24, False, torch.float16)])
+def test_tcgen05_and_mma_sync_kernels_agree_with_oracle(N, K, M, nested, dtype, monkeypatch):
+    """9..64 tokens run the tcgen05 kernel (TMEM accumulator, weights rounded to the activation dtype
+    with their block scale before the MMA) by default and the register-staged mma.sync kernel with
+    B2D_NF4_TC5=0: both meet the oracle bar for fp32 and model-dtype outputs, the tcgen05 kernel is
+    deterministic (split-K partials summed in cluster rank order) and records no timed-out wait."""
+    from b200kernels.nf4_gemm import gemm_errors
+    _, p = make_weight(N, K, nested, seed=N + M)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(M + 2)).to(dtype).to(DEV)
+    odt = "fp16" if dtype == torch.float16 else "bf16"
+    tol = TOL_F32 if dtype == torch.float16 else TOL_BF16
+    ref = reference_matmul(x, p, odt)
+    nf = NF4Weight(p)
+    y5 = nf.matmul(x, out_dtype=torch.float32)
+    y5b = nf.matmul(x, out_dtype=torch.float32)
+    y5h = nf.matmul(x)
+    monkeypatch.setenv("B2D_NF4_TC5", "0")
+    y_old = nf.matmul(x, out_dtype=torch.float32)
+    monkeypatch.delenv("B2D_NF4_TC5")
+    torch.cuda.synchronize()
+    check(y5, ref, tol)
+    check(y_old, ref, tol)
+    check(y5h, ref, tol, unit_slack=dtype == torch.float16)
+    assert torch.equal(y5, y5b)
+    assert gemm_errors(DEV) == 0
