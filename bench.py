@@ -748,12 +748,15 @@ def run_kernels(args):
                         decode_attention(*cases[0], 128 ** -0.5, seqlens=lens)
                     torch.cuda.synchronize()
                     continue
-                us = _graph_time_us([lambda c=c: decode_attention(*c, 128 ** -0.5, seqlens=lens) for c in cases])
                 nbytes = n_keys * 8 * 128 * 2 * 2 + B * 32 * 128 * 2 * 2
-                print(json.dumps({"kernel": "gqa_decode", "B": B, "S": S, "ragged": bool(args.ragged),
-                                  "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
-                                  "pct_peak": round(100 * nbytes / us / 1e3 / peak, 1), "peak_kind": peak_kind}),
-                      flush=True)
+                for ch in [int(c) for c in args.chunks.split(",")]:   # 0: the default split choice
+                    kw = {"chunk": ch} if ch > 0 else {}
+                    us = _graph_time_us([lambda c=c: decode_attention(*c, 128 ** -0.5, seqlens=lens, **kw)
+                                         for c in cases])
+                    print(json.dumps({"kernel": "gqa_decode", "B": B, "S": S, "ragged": bool(args.ragged),
+                                      "chunk": ch or "default", "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
+                                      "pct_peak": round(100 * nbytes / us / 1e3 / peak, 1), "peak_kind": peak_kind}),
+                          flush=True)
                 del cases
                 torch.cuda.empty_cache()
 
@@ -767,6 +770,7 @@ def main():
     ap.add_argument("--prefill-rows", type=int, default=2048, help="rows (batch x prompt) for --kernel prefill")
     ap.add_argument("--contexts", default="128,512,2048,4096")
     ap.add_argument("--ragged", action="store_true")
+    ap.add_argument("--chunks", default="0", help="attention: keys per split to sweep (0 = the default choice)")
     ap.add_argument("--plain", action="store_true", help="fp32 absmax instead of double quantisation")
     ap.add_argument("--profile-iters", type=int, default=0)
     ap.add_argument("--pdl", action="store_true",

@@ -19,6 +19,8 @@
 //   tile prefetched ahead. Warps of a CTA take interleaved tiles and merge through shared memory.
 // Workspace per (b, h, split): unnormalised O[D] (fp32) and (m, l) with m in the log2 domain.
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include <atomic>
 #include <mutex>
@@ -332,6 +334,235 @@ __global__ void __launch_bounds__(D) gqa_combine_kernel(const AttnArgs a) {
   out[d] = Dt<OT>::from_f32(den > 0.f ? num / den : 0.f);
 }
 
+// ------------------------------------------------------------------------------------------------
+// Streaming variant of the partial kernel (the default for two-kernel launches): the same CTA grid, split
+// and workspace format, with K and V staged through shared memory so that far more bytes are in flight.
+//  * A stage is 64 keys of K and of V (32 KB at D = 128), copied by every thread with 16-byte cp.async
+//    (16 threads per 256-byte key row: whole lines), keys past the split's end zero-filled without a
+//    global read. Three stages per CTA, two CTAs per SM: up to 128 KB in flight per SM.
+//  * 16-byte chunk c of key row r sits at chunk c ^ (r & 7), so the ldmatrix reads below (8 key rows of
+//    one chunk column at a time) hit 8 distinct bank groups.
+//  * Warp w takes keys [16w, 16w + 16) of each stage. S = Q K^T: Q (the G heads as MMA rows) in
+//    registers in natural head-dim order, K as the B operand by ldmatrix.x4 (rows = keys, two k-steps of
+//    one 8-key tile per instruction). O += P V: P from the S accumulator, V as the B operand by
+//    ldmatrix.x4.trans (two 8-column d tiles per instruction). Online softmax in the log2 domain as in the
+//    register kernel; the warps meet in shared memory at the end and write one partial per split.
+constexpr int kStreamKeys = 64;
+constexpr int kStreamStages = 3;
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+
+template <int D>
+constexpr size_t stream_smem_bytes() {
+  return static_cast<size_t>(kStreamStages) * 2 * kStreamKeys * D * 2;
+}
+
+template <typename T, int D, bool TWO_HALVES>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const AttnArgs a) {
+  constexpr int KSTEPS = D / 16;        // MMA k-steps over the head dim (S = Q K^T)
+  constexpr int NTILES = D / 8;         // n8 output tiles of O
+  constexpr int CH = D / 8;             // 16-byte chunks per key row
+  constexpr uint32_t ROWB = D * 2;      // bytes per key row
+  constexpr uint32_t TILEB = kStreamKeys * ROWB;   // K (or V) bytes of one stage
+  constexpr int ROWS = TWO_HALVES ? 16 : 8;
+  constexpr int OPAD = D + 8;           // merge-buffer row stride in floats (spreads rows over the banks)
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float s_m[kAttnWarps][ROWS], s_l[kAttnWarps][ROWS];
+
+  pdl_wait();   // no-op unless launched as a programmatic dependent
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int len = seqlen_of(a, b);
+  const int t_begin = split * a.chunk;
+  if (t_begin >= len) return;   // this split holds no keys; the combine skips it
+  const int t_end = min(t_begin + a.chunk, len);
+
+  // ---- Q fragments (rows = heads of this KV group), natural head-dim order
+  uint32_t qa[KSTEPS][4];
+  {
+    const T* qb = static_cast<const T*>(a.q) + b * a.sq_b;
+    const int h0 = kvh * a.G + g, h1 = kvh * a.G + g + 8;
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(qb + static_cast<int64_t>(h0) * a.sq_h);
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(qb + static_cast<int64_t>(h1) * a.sq_h);
+    const bool v0 = g < a.G, v1 = TWO_HALVES && g + 8 < a.G;
+#pragma unroll
+    for (int j = 0; j < KSTEPS; ++j) {
+      qa[j][0] = v0 ? __ldg(q0 + 8 * j + tq) : 0u;       // d = 16j + 2tq, +1
+      qa[j][2] = v0 ? __ldg(q0 + 8 * j + 4 + tq) : 0u;   // d = 16j + 8 + 2tq, +1
+      qa[j][1] = v1 ? __ldg(q1 + 8 * j + tq) : 0u;
+      qa[j][3] = v1 ? __ldg(q1 + 8 * j + 4 + tq) : 0u;
+    }
+  }
+  const T* kbase = static_cast<const T*>(a.k) + b * a.sk_b + kvh * a.sk_h;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.sv_b + kvh * a.sv_h;
+  const uint32_t sbase = smem_u32(smem);
+  const int nst = (t_end - t_begin + kStreamKeys - 1) / kStreamKeys;
+
+  // copies of stage `it` into buffer `bf` (every thread: 64 keys x CH chunks of K and of V)
+  auto issue = [&](int it, int bf) {
+    const uint32_t kdst = sbase + static_cast<uint32_t>(bf) * 2 * TILEB, vdst = kdst + TILEB;
+    const int t0 = t_begin + it * kStreamKeys;
+#pragma unroll
+    for (int i = 0; i < kStreamKeys * CH / (kAttnWarps * 32); ++i) {
+      const int ci = tid + i * kAttnWarps * 32;
+      const int r = ci / CH, c = ci % CH;
+      const int tok = t0 + r;
+      const bool ok = tok < t_end;
+      const int tk = ok ? tok : t_begin;
+      const uint32_t off = static_cast<uint32_t>(r) * ROWB + static_cast<uint32_t>((c ^ (r & 7)) * 16);
+      cp_async16_zfill(kdst + off, kbase + static_cast<int64_t>(tk) * a.sk_s + c * 8, ok);
+      cp_async16_zfill(vdst + off, vbase + static_cast<int64_t>(tk) * a.sv_s + c * 8, ok);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kStreamStages - 1; ++i) {
+    if (i < nst) issue(i, i);
+    cp_async_commit();
+  }
+
+  float o[NTILES][4];
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};   // rows g, g+8 (log2 domain)
+  float l_run[2] = {0.f, 0.f};               // per-thread partial sums over its keys
+
+  // ldmatrix lane roles: matrix mi = lane / 8, row ri = lane % 8
+  const int mi = lane >> 3, ri = lane & 7;
+  for (int it = 0; it < nst; ++it) {
+    cp_async_wait<kStreamStages - 2>();   // this thread's copies of stage `it` have landed
+    __syncthreads();                      // everyone's; and every warp is done with stage it - 1
+    if (it + kStreamStages - 1 < nst) issue(it + kStreamStages - 1, (it + kStreamStages - 1) % kStreamStages);
+    cp_async_commit();
+    const int key0 = t_begin + it * kStreamKeys + 16 * warp;   // this warp's first key
+    if (key0 >= t_end) continue;   // warp-uniform: all its keys are past the end
+    const uint32_t kbuf = sbase + static_cast<uint32_t>(it % kStreamStages) * 2 * TILEB, vbuf = kbuf + TILEB;
+
+    // S for keys key0 + [0, 8) (s[0]) and key0 + [8, 16) (s[1])
+    float s[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      s[h][0] = s[h][1] = s[h][2] = s[h][3] = 0.f;
+      const int r = 16 * warp + 8 * h + ri;   // key row in the stage
+#pragma unroll
+      for (int j = 0; j < KSTEPS; j += 2) {
+        const int c = 2 * j + mi;   // chunks 2j, 2j+1 (k-step j), 2j+2, 2j+3 (k-step j+1)
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbuf + static_cast<uint32_t>(r) * ROWB + static_cast<uint32_t>((c ^ (r & 7)) * 16), b0, b1, b2, b3);
+        Mma<T>::run(s[h], qa[j][0], qa[j][1], qa[j][2], qa[j][3], b0, b1);
+        Mma<T>::run(s[h], qa[j + 1][0], qa[j + 1][1], qa[j + 1][2], qa[j + 1][3], b2, b3);
+      }
+    }
+    // scale, mask, online softmax
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int tok = key0 + h * 8 + 2 * tq + (c & 1);
+        s[h][c] = tok < t_end ? s[h][c] * a.scale_log2 : -INFINITY;
+        tmax[c >> 1] = fmaxf(tmax[c >> 1], s[h][c]);
+      }
+    }
+    float alpha[2], msafe[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
+      const float m_new = fmaxf(m_run[r], tmax[r]);
+      msafe[r] = m_new == -INFINITY ? 0.f : m_new;
+      alpha[r] = exp2f(m_run[r] - msafe[r]);
+      m_run[r] = m_new;
+    }
+    uint32_t pa[4];
+    {
+      float p[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) p[h][c] = exp2f(s[h][c] - msafe[c >> 1]);
+      l_run[0] = l_run[0] * alpha[0] + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
+      l_run[1] = l_run[1] * alpha[1] + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+      pa[0] = Dt<T>::pack2(p[0][0], p[0][1]);   // row g,   keys 2t, 2t+1
+      pa[1] = Dt<T>::pack2(p[0][2], p[0][3]);   // row g+8
+      pa[2] = Dt<T>::pack2(p[1][0], p[1][1]);   // row g,   keys 8+2t, 9+2t
+      pa[3] = Dt<T>::pack2(p[1][2], p[1][3]);
+    }
+    // O = alpha*O + P V; V tiles by ldmatrix.trans: matrices (d tile 2p + mi/2, key half mi%2)
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n) {
+      o[n][0] *= alpha[0]; o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int np = 0; np < NTILES; np += 2) {
+      const int r = 16 * warp + 8 * (mi & 1) + ri, c = np + (mi >> 1);
+      uint32_t v0, v1, v2, v3;
+      ldsm_x4_t(vbuf + static_cast<uint32_t>(r) * ROWB + static_cast<uint32_t>((c ^ (r & 7)) * 16), v0, v1, v2, v3);
+      Mma<T>::run(o[np], pa[0], pa[1], pa[2], pa[3], v0, v1);
+      Mma<T>::run(o[np + 1], pa[0], pa[1], pa[2], pa[3], v2, v3);
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();   // the stage buffers become the merge buffer
+
+  // ---- per-warp results -> shared memory (rows g, g+8; thread owns d = 8n + 2t, +1)
+  float* s_o = reinterpret_cast<float*>(smem);   // [kAttnWarps][ROWS][OPAD]
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+#pragma unroll
+  for (int r = 0; r < (TWO_HALVES ? 2 : 1); ++r) {
+    const int row = g + 8 * r;
+    if (tq == 0) {
+      s_m[warp][row] = m_run[r];
+      s_l[warp][row] = l_run[r];
+    }
+    float* dst = s_o + (warp * ROWS + row) * OPAD + 2 * tq;
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n)
+      *reinterpret_cast<float2*>(dst + 8 * n) = make_float2(o[n][2 * r], o[n][2 * r + 1]);
+  }
+  __syncthreads();
+
+  // ---- merge the warps and write this split's partial (a warp that saw no keys has m = -inf, l = 0)
+  const int nrows = min(a.G, ROWS);
+  const int64_t slot0 = (static_cast<int64_t>(b) * a.H + kvh * a.G) * a.nsplit + split;
+  for (int idx = tid; idx < nrows * D; idx += kAttnWarps * 32) {
+    const int row = idx / D, d = idx - row * D;
+    float mx = s_m[0][row];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_m[w][row]);
+    float acc = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float e = s_m[w][row] == -INFINITY ? 0.f : exp2f(s_m[w][row] - mx);
+      acc += e * s_o[(w * ROWS + row) * OPAD + d];
+      l += e * s_l[w][row];
+    }
+    const int64_t slot = slot0 + static_cast<int64_t>(row) * a.nsplit;
+    a.acc[slot * D + d] = acc;
+    if (d == 0) {
+      a.ml[slot * 2] = mx;
+      a.ml[slot * 2 + 1] = l;
+    }
+  }
+  pdl_launch_dependents();
+}
+
 int check_attn(int B, int H, int KVH, int S, int D, int dtype) {
   if (B < 0 || H < 0 || KVH < 0 || S < 0) return B2D_ERR_ARG;
   if (dtype != B2D_F16 && dtype != B2D_BF16) return B2D_ERR_DTYPE;
@@ -368,7 +599,43 @@ int launch_partial_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(gqa_partial_kernel<T, D, false>, grid, dim3(kAttnWarps * 32), 0, s, pdl, a);
 }
 
+// Which partial kernel serves a two-kernel launch: B2D_ATTN_KERNEL=stream / reg in the environment selects
+// the streaming or the register-prefetch kernel (read at every call, for comparisons); otherwise
+// kStreamByDefault decides. Single-launch combines always run the register-prefetch kernel, which
+// implements them.
+constexpr bool kStreamByDefault = false;
+bool stream_attn_enabled() {
+  const char* v = std::getenv("B2D_ATTN_KERNEL");
+  if (v && std::strcmp(v, "reg") == 0) return false;
+  if (v && std::strcmp(v, "stream") == 0) return true;
+  return kStreamByDefault;
+}
+
+template <typename T, int D, bool TWO>
+int launch_stream_tt(const AttnArgs& a, cudaStream_t s, bool pdl) {
+  auto kern = gqa_stream_kernel<T, D, TWO>;
+  constexpr size_t smem = stream_smem_bytes<D>();
+  static bool configured[64] = {false};   // per device; setting it twice is harmless
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B2D_ERR_DEVICE;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) { set_cuda_error(e); return B2D_ERR_LAUNCH; }
+    configured[dev] = true;
+  }
+  return launch_kernel(kern, dim3(a.nsplit, a.KVH, a.B), dim3(kAttnWarps * 32), smem, s, pdl, a);
+}
+
+template <typename T, int D>
+int launch_stream_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
+  return a.G > 8 ? launch_stream_tt<T, D, true>(a, s, pdl) : launch_stream_tt<T, D, false>(a, s, pdl);
+}
+
 int launch_partial(const AttnArgs& a, int D, int dtype, cudaStream_t s, bool pdl = false) {
+  if (!a.fused && stream_attn_enabled()) {
+    if (dtype == B2D_F16) return D == 64 ? launch_stream_t<__half, 64>(a, s, pdl) : launch_stream_t<__half, 128>(a, s, pdl);
+    return D == 64 ? launch_stream_t<__nv_bfloat16, 64>(a, s, pdl) : launch_stream_t<__nv_bfloat16, 128>(a, s, pdl);
+  }
   if (dtype == B2D_F16) {
     if (D == 64) return launch_partial_t<__half, 64>(a, s, pdl);
     return launch_partial_t<__half, 128>(a, s, pdl);
