@@ -54,8 +54,11 @@ enum { B2D_F16 = 0, B2D_BF16 = 1, B2D_F32 = 2 };
  *                       stream, so their prefetch may start before the previous kernel completes.
  *   B2D_ATTN_FUSED_COMBINE  (attention) one launch: the last split CTA of each (sequence, KV head)
  *                       to finish does the log-sum-exp combine (no second kernel). Applies when
- *                       nsplit <= 64 and B*KVH <= 16384; otherwise the two-kernel path runs. */
-enum { B2D_LAUNCH_PDL = 1, B2D_STATIC_WEIGHTS = 2, B2D_ATTN_FUSED_COMBINE = 4 };
+ *                       nsplit <= 64 and B*KVH <= 16384; otherwise the two-kernel path runs.
+ *   B2D_KV_STATIC_PREFIX  (attention, with B2D_LAUNCH_PDL) the preceding kernels of the stream write
+ *                       at most the last cached key/value of each sequence (a decode step's append),
+ *                       so the keys before it may be prefetched before the previous kernel completes. */
+enum { B2D_LAUNCH_PDL = 1, B2D_STATIC_WEIGHTS = 2, B2D_ATTN_FUSED_COMBINE = 4, B2D_KV_STATIC_PREFIX = 8 };
 
 const char* b2d_strerror(int status);
 /* Text of the last CUDA error seen by a launch in this thread ("" if none). */

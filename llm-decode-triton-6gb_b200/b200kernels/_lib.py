@@ -16,7 +16,7 @@ F16, BF16, F32 = 0, 1, 2
 
 _p, _i64, _i32, _f32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 
-LAUNCH_PDL, STATIC_WEIGHTS, ATTN_FUSED_COMBINE = 1, 2, 4   # launch flags
+LAUNCH_PDL, STATIC_WEIGHTS, ATTN_FUSED_COMBINE, KV_STATIC_PREFIX = 1, 2, 4, 8   # launch flags
 SEG_INDEPENDENT, SEG_SILU_MUL, SEG_ALLREDUCE = 0, 1, 2   # b2d_nf4_gemm_multi modes
 
 

@@ -196,8 +196,9 @@ class DecodeEngine:
             q3 = self.q.view(B, H, D)
             rope_kv_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, q3, self.k_cache[i], self.v_cache[i],
                            self.seqlens, flags=PDL)
+            # the append above writes only each sequence's newest key/value: the older ones may be prefetched
             decode_attention(q3.view(B, H, 1, D), self.k_cache[i], self.v_cache[i], self.scale, seqlens=self.seqlens,
-                             out=self.attn, flags=PDL)
+                             out=self.attn, flags=PDL | _lib.KV_STATIC_PREFIX)
             a2 = self.attn.view(B, H * D)
             if arf:
                 g["o"].matmul(a2, flags=STATIC, epilogue=tp.epilogue(2 * i))

@@ -52,6 +52,7 @@ struct AttnArgs {
   int* counters;   // [B*KVH], zero between launches
   int fused;       // 1: the last split CTA of each (b, kvh) combines and writes out
   int out_f32;     // fused: out is fp32 (else the input dtype)
+  int kv_prefix;   // 1: keys before each sequence's newest one may be read before the dependency wait
 };
 
 template <typename T>
@@ -380,13 +381,55 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_m[kAttnWarps][ROWS], s_l[kAttnWarps][ROWS];
 
-  pdl_wait();   // no-op unless launched as a programmatic dependent
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
-  const int len = seqlen_of(a, b);
   const int t_begin = split * a.chunk;
-  if (t_begin >= len) return;   // this split holds no keys; the combine skips it
+  const T* kbase = static_cast<const T*>(a.k) + b * a.sk_b + kvh * a.sk_h;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.sv_b + kvh * a.sv_h;
+  const uint32_t sbase = smem_u32(smem);
+
+  // copies of stage `it` into buffer `bf` (every thread: 64 keys x CH chunks of K and of V); keys at or
+  // past `lim` are zero-filled without a global read
+  auto issue = [&](int it, int bf, int lim) {
+    const uint32_t kdst = sbase + static_cast<uint32_t>(bf) * 2 * TILEB, vdst = kdst + TILEB;
+    const int t0 = t_begin + it * kStreamKeys;
+#pragma unroll
+    for (int i = 0; i < kStreamKeys * CH / (kAttnWarps * 32); ++i) {
+      const int ci = tid + i * kAttnWarps * 32;
+      const int r = ci / CH, c = ci % CH;
+      const int tok = t0 + r;
+      const bool ok = tok < lim;
+      const int tk = ok ? tok : t_begin;
+      const uint32_t off = static_cast<uint32_t>(r) * ROWB + static_cast<uint32_t>((c ^ (r & 7)) * 16);
+      cp_async16_zfill(kdst + off, kbase + static_cast<int64_t>(tk) * a.sk_s + c * 8, ok);
+      cp_async16_zfill(vdst + off, vbase + static_cast<int64_t>(tk) * a.sv_s + c * 8, ok);
+    }
+  };
+  // With a static prefix (a decode step's append writes only each sequence's newest key/value), whole
+  // stages below the newest key start before the dependency wait. The length read here may be this step's
+  // or the previous one's (the appending kernel may not have written it yet): both bound keys that no
+  // preceding kernel writes.
+  int pre = 0;
+  if (a.kv_prefix) {
+    int seen = a.S;
+    if (a.seqlens) {
+      asm volatile("ld.volatile.global.s32 %0, [%1];\n" : "=r"(seen) : "l"(a.seqlens + b) : "memory");
+      seen = seen < 0 ? 0 : (seen > a.S ? a.S : seen);
+    }
+    const int lim = min(t_begin + a.chunk, seen - 1);
+    while (pre < kStreamStages - 1 && t_begin + (pre + 1) * kStreamKeys <= lim) ++pre;
+    for (int i = 0; i < pre; ++i) {
+      issue(i, i, lim);
+      cp_async_commit();
+    }
+  }
+  pdl_wait();   // no-op unless launched as a programmatic dependent
+  const int len = seqlen_of(a, b);
+  if (t_begin >= len) {   // this split holds no keys; the combine skips it
+    cp_async_wait<0>();
+    return;
+  }
   const int t_end = min(t_begin + a.chunk, len);
 
   // ---- Q fragments (rows = heads of this KV group), natural head-dim order
@@ -405,30 +448,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
       qa[j][3] = v1 ? __ldg(q1 + 8 * j + 4 + tq) : 0u;
     }
   }
-  const T* kbase = static_cast<const T*>(a.k) + b * a.sk_b + kvh * a.sk_h;
-  const T* vbase = static_cast<const T*>(a.v) + b * a.sv_b + kvh * a.sv_h;
-  const uint32_t sbase = smem_u32(smem);
   const int nst = (t_end - t_begin + kStreamKeys - 1) / kStreamKeys;
-
-  // copies of stage `it` into buffer `bf` (every thread: 64 keys x CH chunks of K and of V)
-  auto issue = [&](int it, int bf) {
-    const uint32_t kdst = sbase + static_cast<uint32_t>(bf) * 2 * TILEB, vdst = kdst + TILEB;
-    const int t0 = t_begin + it * kStreamKeys;
-#pragma unroll
-    for (int i = 0; i < kStreamKeys * CH / (kAttnWarps * 32); ++i) {
-      const int ci = tid + i * kAttnWarps * 32;
-      const int r = ci / CH, c = ci % CH;
-      const int tok = t0 + r;
-      const bool ok = tok < t_end;
-      const int tk = ok ? tok : t_begin;
-      const uint32_t off = static_cast<uint32_t>(r) * ROWB + static_cast<uint32_t>((c ^ (r & 7)) * 16);
-      cp_async16_zfill(kdst + off, kbase + static_cast<int64_t>(tk) * a.sk_s + c * 8, ok);
-      cp_async16_zfill(vdst + off, vbase + static_cast<int64_t>(tk) * a.sv_s + c * 8, ok);
-    }
-  };
-#pragma unroll
-  for (int i = 0; i < kStreamStages - 1; ++i) {
-    if (i < nst) issue(i, i);
+  for (int i = pre; i < kStreamStages - 1; ++i) {
+    if (i < nst) issue(i, i, t_end);
     cp_async_commit();
   }
 
@@ -443,7 +465,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
   for (int it = 0; it < nst; ++it) {
     cp_async_wait<kStreamStages - 2>();   // this thread's copies of stage `it` have landed
     __syncthreads();                      // everyone's; and every warp is done with stage it - 1
-    if (it + kStreamStages - 1 < nst) issue(it + kStreamStages - 1, (it + kStreamStages - 1) % kStreamStages);
+    if (it + kStreamStages - 1 < nst) issue(it + kStreamStages - 1, (it + kStreamStages - 1) % kStreamStages, t_end);
     cp_async_commit();
     const int key0 = t_begin + it * kStreamKeys + 16 * warp;   // this warp's first key
     if (key0 >= t_end) continue;   // warp-uniform: all its keys are past the end
@@ -785,6 +807,7 @@ extern "C" int b2d_gqa_decode_ex(const void* q, int64_t sq_b, int64_t sq_h, cons
     return st;
   if (nsplit > 65535 || KVH > 65535 || B > 65535) return B2D_ERR_SHAPE;
   a.out = out; a.so_b = so_b; a.so_h = so_h;
+  a.kv_prefix = (flags & B2D_KV_STATIC_PREFIX) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((flags & B2D_ATTN_FUSED_COMBINE) && nsplit <= kMaxFusedSplits && B * KVH <= kMaxAttnCounters) {
     a.fused = 1;

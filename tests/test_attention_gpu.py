@@ -193,3 +193,22 @@ def test_streaming_and_register_kernels_agree_with_oracle(B, H, KVH, S, D, dtype
     check(y1, ref, tol)
     check(yr, ref, tol)
     assert torch.equal(y1, y2)
+
+
+def test_static_prefix_flag_matches_oracle():
+    """B2D_KV_STATIC_PREFIX (with B2D_LAUNCH_PDL) lets the streaming kernel fetch whole stages below each
+    sequence's newest key before the dependency wait; right after a kernel that wrote the cache the result
+    is the same: the oracle bar on ragged lengths, and equal to the plain launch."""
+    q, k, v, sl = rand_case(8, 32, 8, 2048, 128, seed=11,
+                            lens=[2048, 1, 64, 65, 700, 1500, 129, 1024])
+    ref = oracle(q, k, v, sl)
+    qd, kd, vd, sld = q.to(DEV), k.to(DEV), v.to(DEV), sl.to(DEV)
+    plain = decode_attention(qd, kd, vd, 128 ** -0.5, seqlens=sld, out_dtype=torch.float32)
+    kd2, vd2 = torch.empty_like(kd), torch.empty_like(vd)
+    kd2.copy_(kd)   # the preceding kernels of the stream write the caches
+    vd2.copy_(vd)
+    pre = decode_attention(qd, kd2, vd2, 128 ** -0.5, seqlens=sld, out_dtype=torch.float32,
+                           flags=_lib.LAUNCH_PDL | _lib.KV_STATIC_PREFIX)
+    torch.cuda.synchronize()
+    check(pre, ref)
+    assert torch.equal(pre, plain)
