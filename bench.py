@@ -6,7 +6,8 @@ Workload (N=1): random-init Mistral-7B-shaped model (32 layers, hidden 4096, 32 
 head_dim 128, SwiGLU 14336, vocab 32768, RMSNorm eps 1e-5, RoPE theta 1e6), every decoder linear NF4
 (blocksize 64, double-quantised scales, blocksize 256), fp16 activations; B seeded random prompts of
 256 tokens are prefilled, then greedy decode. One step = one decode token for every sequence through
-all 32 layers (7 fused NF4 dequant+matmul launches and one split-K attention + combine per layer),
+all 32 layers (7 fused NF4 dequant+matmul launches and one split-K attention + combine per layer, the
+step's RoPE + KV append inside the attention launch),
 replayed as a CUDA graph. The 3.9 GB of weights streamed per step exceed the 126 MB L2, so no flush
 is needed between steps.
 
@@ -506,10 +507,12 @@ def run_b200(args):
     peak, peak_kind = measured_peaks()
     achieved = alg / (us * 1e-6) / 1e9
 
-    # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE + KV append, attention partial +
-    # combine and the NF4 launches (q/k/v, o, gate/up, down at B <= 8; else 7 NF4 launches and SiLU*mul),
-    # plus the all-reduces under TP; plus the final add+RMSNorm
-    per_layer = (5 + 4) if eng.pair else (5 + 7 + 1)
+    # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE + KV append (inside the attention
+    # partial launch when the engine folds it in), attention partial + combine and the NF4 launches (q/k/v,
+    # o, gate/up, down at B <= 8; else 7 NF4 launches and SiLU*mul), plus the all-reduces under TP; plus the
+    # final add+RMSNorm
+    glue = 4 if eng.attn_append else 5
+    per_layer = (glue + 4) if eng.pair else (glue + 7 + 1)
     if tp is not None and not eng.ar_fused:   # fused: the GEMMs push, the add+RMSNorm launches sum
         per_layer += 2
     launches_per_step = args.layers * per_layer + 1 + (1 if eng.lm_fused else 0)   # + final norm (+ lm_head)

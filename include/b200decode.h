@@ -235,6 +235,26 @@ int b2d_gqa_decode_ex(const void* q, int64_t sq_b, int64_t sq_h,
                       void* workspace, size_t workspace_bytes,
                       void* out, int64_t so_b, int64_t so_h, int out_dtype, int flags, void* stream);
 
+/* Decode-step attention with the step's RoPE and KV-cache append folded into the partial kernel (no
+ * counterpart in the reference, whose decode step rotates q/k and appends to the cache with torch ops
+ * before its attention kernel). q [B, H*D] (row stride ldq) and k_new / v_new [B, KVH*D] are this step's
+ * projection outputs before RoPE; pos [B] (int64) the step's position of each sequence, written before
+ * the step; rcos / rsin [>= S, D] (row stride ld_cs) the rotary tables. The launch rotates q in
+ * registers, writes the rotated key and the value at position pos[b] of k_cache / v_cache (the HF
+ * layout [B, KVH, S, D] with the given strides), writes seqlens[b] = pos[b] + 1 (0 for a position
+ * outside [0, S)) and attends over keys [0, pos[b]]; the keys before pos[b] are fetched before the
+ * previous kernel completes under B2D_LAUNCH_PDL, so the preceding kernels must not write them. Same
+ * rounding as b2d_rope_kv_append followed by b2d_gqa_decode_ex: the outputs and the caches are
+ * bit-identical. Default split choice; workspace as b2d_gqa_decode. flags: B2D_LAUNCH_PDL. */
+int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_new, int64_t ldk,
+                          const void* v_new, int64_t ldv, const int64_t* pos,
+                          const void* rcos, const void* rsin, int64_t ld_cs,
+                          void* k_cache, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                          void* v_cache, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                          int32_t* seqlens, int B, int H, int KVH, int S, int D, float scale, int dtype,
+                          void* workspace, size_t workspace_bytes,
+                          void* out, int64_t so_b, int64_t so_h, int out_dtype, int flags, void* stream);
+
 /* ================================================================ decode-step glue
  * The small per-layer operations of a Mistral decoder layer around the two hot paths, as kernels
  * that take B2D_LAUNCH_PDL (no counterpart in the reference, which runs these as separate torch ops:

@@ -21,13 +21,15 @@ library GEMM for the many-row linears); the prompt's K/V are then copied into th
 """
 from __future__ import annotations
 
+import os
+
 import torch
 from transformers import MistralConfig, MistralForCausalLM
 from transformers.cache_utils import DynamicCache
 from transformers.models.mistral.modeling_mistral import apply_rotary_pos_emb
 
 from . import _lib
-from .decode_attention import decode_attention
+from .decode_attention import decode_attention, decode_attention_append
 from .glue import add_rmsnorm, rope_kv_append, silu_mul
 from .lm_head import MAX_M as LM_MAX_M, lm_head_argmax, merge_keys
 from .linear4bit import quantize_model_linears
@@ -166,6 +168,9 @@ class DecodeEngine:
         self.g_out = None if self.pair else z(B, inter)
         self.down_out = z(B, hid)
         self.seqlens = torch.zeros(B, dtype=torch.int32, device=dev)
+        # the streaming attention kernel also applies RoPE and appends the step's K/V (one launch fewer per
+        # layer); B2D_ATTN_KERNEL=reg selects the separate rotary kernel + register-prefetch attention
+        self.attn_append = os.environ.get("B2D_ATTN_KERNEL", "stream") != "reg"
         # rotary tables for every cache position, computed by the model's own rotary module
         pos = torch.arange(self.S, device=dev).view(1, -1)
         cos, sin = self.model.model.rotary_emb(self.r.view(B, 1, hid)[:1], pos)
@@ -193,12 +198,16 @@ class DecodeEngine:
                 g["qkv"].matmul(self.xn, [self.q, self.k, self.v], flags=STATIC)
             else:
                 w["q"].matmul(self.xn, out=self.q); w["k"].matmul(self.xn, out=self.k); w["v"].matmul(self.xn, out=self.v)
-            q3 = self.q.view(B, H, D)
-            rope_kv_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, q3, self.k_cache[i], self.v_cache[i],
-                           self.seqlens, flags=PDL)
-            # the append above writes only each sequence's newest key/value: the older ones may be prefetched
-            decode_attention(q3.view(B, H, 1, D), self.k_cache[i], self.v_cache[i], self.scale, seqlens=self.seqlens,
-                             out=self.attn, flags=PDL | _lib.KV_STATIC_PREFIX)
+            if self.attn_append:   # RoPE + KV append inside the attention launch
+                decode_attention_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, self.k_cache[i],
+                                        self.v_cache[i], self.scale, self.seqlens, self.attn, flags=PDL)
+            else:
+                q3 = self.q.view(B, H, D)
+                rope_kv_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, q3, self.k_cache[i],
+                               self.v_cache[i], self.seqlens, flags=PDL)
+                # the append above writes only each sequence's newest key/value: the older ones may be prefetched
+                decode_attention(q3.view(B, H, 1, D), self.k_cache[i], self.v_cache[i], self.scale,
+                                 seqlens=self.seqlens, out=self.attn, flags=PDL | _lib.KV_STATIC_PREFIX)
             a2 = self.attn.view(B, H * D)
             if arf:
                 g["o"].matmul(a2, flags=STATIC, epilogue=tp.epilogue(2 * i))

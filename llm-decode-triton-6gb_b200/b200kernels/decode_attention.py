@@ -87,3 +87,27 @@ def decode_attention(q, k, v, scale=None, chunk=None, block_s=None, seqlens=None
     else:
         _lib.call("b2d_gqa_decode", *args, _lib.stream_ptr(q.device))
     return out
+
+
+def decode_attention_append(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos: torch.Tensor,
+                            cos: torch.Tensor, sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            scale: float, seqlens: torch.Tensor, out: torch.Tensor, flags: int = 0) -> torch.Tensor:
+    """One decode step's attention with its RoPE and KV append folded in (``b2d_gqa_decode_append``):
+    q [B, H*D], k_new / v_new [B, KVH*D] (projection outputs before RoPE), pos int64 [B], cos / sin
+    [>= S, D], k_cache / v_cache [B, KVH, S, D] (the new key and value are written at ``pos``),
+    seqlens int32 [B] (set to pos + 1), out [B, 1, H, D]. The same numbers as ``rope_kv_append``
+    followed by ``decode_attention``."""
+    B, KVH, S, D = k_cache.shape
+    H = q.shape[1] // D
+    assert pos.dtype == torch.int64 and seqlens.dtype == torch.int32 and cos.shape[0] >= S and sin.shape == cos.shape
+    nsplit, _ = plan_splits(B, KVH, S)
+    nbytes = _lib.load().b2d_gqa_workspace_bytes(B, H, nsplit, D)
+    ws = attention_workspace(q.device, nbytes)
+    _lib.call("b2d_gqa_decode_append", q.data_ptr(), q.stride(0), k_new.data_ptr(), k_new.stride(0),
+              v_new.data_ptr(), v_new.stride(0), pos.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+              k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+              v_cache.data_ptr(), v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+              seqlens.data_ptr(), B, H, KVH, S, D, float(scale), _lib.dtype_code(q.dtype), ws.data_ptr(), ws.numel(),
+              out.data_ptr(), out.stride(0), out.stride(2), _lib.dtype_code(out.dtype), int(flags),
+              _lib.stream_ptr(q.device))
+    return out

@@ -53,6 +53,14 @@ struct AttnArgs {
   int fused;       // 1: the last split CTA of each (b, kvh) combines and writes out
   int out_f32;     // fused: out is fp32 (else the input dtype)
   int kv_prefix;   // 1: keys before each sequence's newest one may be read before the dependency wait
+  // append mode (b2d_gqa_decode_append): q holds the projection output before RoPE; the kernel rotates it,
+  // rotates and appends this step's key/value at position pos[b], and writes seqlens[b] = pos[b] + 1
+  int append;
+  const void* k_new; int64_t ldk_new;
+  const void* v_new; int64_t ldv_new;
+  const int64_t* pos;
+  const void* rcos; const void* rsin; int64_t ld_cs;
+  int32_t* seqlens_out;
 };
 
 template <typename T>
@@ -364,6 +372,36 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
 }
 
+// Coherent 4-byte load in volatile asm (data of the preceding kernel: stays below the dependency wait).
+__device__ __forceinline__ uint32_t ld_act_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+template <typename T>
+__device__ __forceinline__ float rnd16(float v) { return Dt<T>::to_f32(Dt<T>::from_f32(v)); }
+// RoPE of two element pairs (x1 = lo[e] at d, x2 = hi[e] at d + D/2) with the rounding of the rotary
+// kernel (q * cos + rotate_half(q) * sin, every product rounded to T, the sum rounded to T).
+template <typename T>
+__device__ __forceinline__ void rope_pair(uint32_t& lo, uint32_t& hi, uint32_t c1, uint32_t c2, uint32_t s1,
+                                          uint32_t s2) {
+  const T* xl = reinterpret_cast<const T*>(&lo);
+  const T* xh = reinterpret_cast<const T*>(&hi);
+  const T* pc1 = reinterpret_cast<const T*>(&c1);
+  const T* pc2 = reinterpret_cast<const T*>(&c2);
+  const T* ps1 = reinterpret_cast<const T*>(&s1);
+  const T* ps2 = reinterpret_cast<const T*>(&s2);
+  float o1[2], o2[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float x1 = Dt<T>::to_f32(xl[e]), x2 = Dt<T>::to_f32(xh[e]);
+    o1[e] = rnd16<T>(x1 * Dt<T>::to_f32(pc1[e])) + rnd16<T>(-x2 * Dt<T>::to_f32(ps1[e]));
+    o2[e] = rnd16<T>(x2 * Dt<T>::to_f32(pc2[e])) + rnd16<T>(x1 * Dt<T>::to_f32(ps2[e]));
+  }
+  lo = Dt<T>::pack2(o1[0], o1[1]);
+  hi = Dt<T>::pack2(o2[0], o2[1]);
+}
+
 template <int D>
 constexpr size_t stream_smem_bytes() {
   return static_cast<size_t>(kStreamStages) * 2 * kStreamKeys * D * 2;
@@ -409,11 +447,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
   // With a static prefix (a decode step's append writes only each sequence's newest key/value), whole
   // stages below the newest key start before the dependency wait. The length read here may be this step's
   // or the previous one's (the appending kernel may not have written it yet): both bound keys that no
-  // preceding kernel writes.
+  // preceding kernel writes. In append mode the position comes from pos[b], written before the step.
   int pre = 0;
-  if (a.kv_prefix) {
+  int64_t apos = -1;   // append mode: this step's position of sequence b
+  if (a.append) {
+    apos = a.pos[b];
+    if (apos < 0 || apos >= a.S) apos = -1;
+  }
+  if (a.kv_prefix || a.append) {
     int seen = a.S;
-    if (a.seqlens) {
+    if (a.append) {
+      seen = static_cast<int>(apos) + 1;   // 0 for an invalid position
+    } else if (a.seqlens) {
       asm volatile("ld.volatile.global.s32 %0, [%1];\n" : "=r"(seen) : "l"(a.seqlens + b) : "memory");
       seen = seen < 0 ? 0 : (seen > a.S ? a.S : seen);
     }
@@ -425,7 +470,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
     }
   }
   pdl_wait();   // no-op unless launched as a programmatic dependent
-  const int len = seqlen_of(a, b);
+  const int len = a.append ? static_cast<int>(apos) + 1 : seqlen_of(a, b);
+  if (a.append && split == 0 && kvh == 0 && tid == 0) a.seqlens_out[b] = len;
   if (t_begin >= len) {   // this split holds no keys; the combine skips it
     cp_async_wait<0>();
     return;
@@ -442,11 +488,49 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
     const bool v0 = g < a.G, v1 = TWO_HALVES && g + 8 < a.G;
 #pragma unroll
     for (int j = 0; j < KSTEPS; ++j) {
-      qa[j][0] = v0 ? __ldg(q0 + 8 * j + tq) : 0u;       // d = 16j + 2tq, +1
-      qa[j][2] = v0 ? __ldg(q0 + 8 * j + 4 + tq) : 0u;   // d = 16j + 8 + 2tq, +1
-      qa[j][1] = v1 ? __ldg(q1 + 8 * j + tq) : 0u;
-      qa[j][3] = v1 ? __ldg(q1 + 8 * j + 4 + tq) : 0u;
+      qa[j][0] = v0 ? ld_act_u32(q0 + 8 * j + tq) : 0u;       // d = 16j + 2tq, +1
+      qa[j][2] = v0 ? ld_act_u32(q0 + 8 * j + 4 + tq) : 0u;   // d = 16j + 8 + 2tq, +1
+      qa[j][1] = v1 ? ld_act_u32(q1 + 8 * j + tq) : 0u;
+      qa[j][3] = v1 ? ld_act_u32(q1 + 8 * j + 4 + tq) : 0u;
     }
+    if (a.append) {
+      // RoPE in registers, rounded as the rotary kernel rounds: d < D/2 pairs with d + D/2, and both sit in
+      // this lane (k-steps j and j + KSTEPS/2 at the same fragment position)
+      const uint32_t* cs = reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.rcos) + apos * a.ld_cs);
+      const uint32_t* sn = reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.rsin) + apos * a.ld_cs);
+#pragma unroll
+      for (int j = 0; j < KSTEPS / 2; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int w = 8 * j + (r >= 2 ? 4 : 0) + tq;   // u32 index of this fragment's pair
+          rope_pair<T>(qa[j][r], qa[j + KSTEPS / 2][r], __ldg(cs + w), __ldg(cs + w + D / 4), __ldg(sn + w),
+                       __ldg(sn + w + D / 4));
+        }
+    }
+  }
+  if (a.append && t_begin <= len - 1 && len - 1 < t_end) {
+    // this split holds the new position: rotate this step's key and append it and the value to the cache
+    // before any stage that covers it is copied
+    const int64_t p = len - 1;
+    const T* kn = static_cast<const T*>(a.k_new) + b * a.ldk_new + static_cast<int64_t>(kvh) * D;
+    const T* vn = static_cast<const T*>(a.v_new) + b * a.ldv_new + static_cast<int64_t>(kvh) * D;
+    T* kd = const_cast<T*>(kbase) + p * a.sk_s;
+    T* vd = const_cast<T*>(vbase) + p * a.sv_s;
+    const T* cs = static_cast<const T*>(a.rcos) + p * a.ld_cs;
+    const T* sn = static_cast<const T*>(a.rsin) + p * a.ld_cs;
+    if (tid < D / 2) {
+      const int i = tid;
+      const float x1 = Dt<T>::to_f32(kn[i]), x2 = Dt<T>::to_f32(kn[i + D / 2]);
+      const float c1 = Dt<T>::to_f32(cs[i]), c2 = Dt<T>::to_f32(cs[i + D / 2]);
+      const float s1 = Dt<T>::to_f32(sn[i]), s2 = Dt<T>::to_f32(sn[i + D / 2]);
+      kd[i] = Dt<T>::from_f32(rnd16<T>(x1 * c1) + rnd16<T>(-x2 * s1));
+      kd[i + D / 2] = Dt<T>::from_f32(rnd16<T>(x2 * c2) + rnd16<T>(x1 * s2));
+    } else if (tid < D) {
+      const int i = 2 * (tid - D / 2);
+      *reinterpret_cast<uint32_t*>(vd + i) = *reinterpret_cast<const uint32_t*>(vn + i);
+    }
+    __threadfence_block();
+    __syncthreads();
   }
   const int nst = (t_end - t_begin + kStreamKeys - 1) / kStreamKeys;
   for (int i = pre; i < kStreamStages - 1; ++i) {
@@ -825,6 +909,56 @@ extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const v
                               int64_t so_h, int out_dtype, void* stream) {
   return b2d_gqa_decode_ex(q, sq_b, sq_h, k, sk_b, sk_h, sk_s, v, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D, scale,
                            nsplit, chunk, dtype, workspace, workspace_bytes, out, so_b, so_h, out_dtype, 0, stream);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Decode-step attention with the step's RoPE and KV append folded in (no counterpart in the reference,
+// whose decode step rotates and appends with torch ops before calling its attention kernel). One launch of
+// the streaming partial kernel + the combine instead of the rotary/append kernel + both attention kernels.
+extern "C" int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_new, int64_t ldk, const void* v_new,
+                                     int64_t ldv, const int64_t* pos, const void* rcos, const void* rsin,
+                                     int64_t ld_cs, void* k_cache, int64_t sk_b, int64_t sk_h, int64_t sk_s,
+                                     void* v_cache, int64_t sv_b, int64_t sv_h, int64_t sv_s, int32_t* seqlens,
+                                     int B, int H, int KVH, int S, int D, float scale, int dtype, void* workspace,
+                                     size_t workspace_bytes, void* out, int64_t so_b, int64_t so_h, int out_dtype,
+                                     int flags, void* stream) {
+  int st = check_attn(B, H, KVH, S, D, dtype);
+  if (st != B2D_OK) return st;
+  if (out_dtype != dtype && out_dtype != B2D_F32) return B2D_ERR_DTYPE;
+  if (B == 0 || H == 0) return B2D_OK;
+  if (S == 0) return B2D_ERR_SHAPE;
+  if (!q || !k_new || !v_new || !pos || !rcos || !rsin || !k_cache || !v_cache || !seqlens || !out) return B2D_ERR_ARG;
+  if (ldq < static_cast<int64_t>(H) * D || ldk < static_cast<int64_t>(KVH) * D || ldv < static_cast<int64_t>(KVH) * D ||
+      ld_cs < D)
+    return B2D_ERR_SHAPE;
+  if ((st = check_strides(q, ldq, D, k_cache, sk_b, sk_h, sk_s, v_cache, sv_b, sv_h, sv_s)) != B2D_OK) return st;
+  if (!aligned(k_new, 4) || !aligned(v_new, 4) || !aligned(rcos, 4) || !aligned(rsin, 4) || (ldk | ldv | ld_cs) % 2)
+    return B2D_ERR_ALIGN;
+  DeviceInfo di;
+  if ((st = device_info(&di)) != B2D_OK) return st;
+  int nsplit = b2d_gqa_default_splits(B, KVH, S);
+  const int chunk = default_chunk(S, nsplit);
+  nsplit = (S + chunk - 1) / chunk;
+  AttnArgs a;
+  if ((st = fill_args(&a, q, ldq, D, k_cache, sk_b, sk_h, sk_s, v_cache, sv_b, sv_h, sv_s, seqlens, B, H, KVH, S, D,
+                      scale, nsplit, chunk, workspace, workspace_bytes)) != B2D_OK)
+    return st;
+  if (nsplit > 65535 || KVH > 65535 || B > 65535) return B2D_ERR_SHAPE;
+  a.out = out; a.so_b = so_b; a.so_h = so_h;
+  a.append = 1;
+  a.k_new = k_new; a.ldk_new = ldk;
+  a.v_new = v_new; a.ldv_new = ldv;
+  a.pos = pos;
+  a.rcos = rcos; a.rsin = rsin; a.ld_cs = ld_cs;
+  a.seqlens_out = seqlens;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
+  if (dtype == B2D_F16)
+    st = D == 64 ? launch_stream_t<__half, 64>(a, s, pdl) : launch_stream_t<__half, 128>(a, s, pdl);
+  else
+    st = D == 64 ? launch_stream_t<__nv_bfloat16, 64>(a, s, pdl) : launch_stream_t<__nv_bfloat16, 128>(a, s, pdl);
+  if (st != B2D_OK) return st;
+  return launch_combine(a, D, out_dtype, s, true);
 }
 
 // ------------------------------------------------------------------------------------------------

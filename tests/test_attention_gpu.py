@@ -212,3 +212,40 @@ def test_static_prefix_flag_matches_oracle():
     torch.cuda.synchronize()
     check(pre, ref)
     assert torch.equal(pre, plain)
+
+
+@pytest.mark.parametrize("B,H,KVH,S,D,dtype", [(8, 32, 8, 357, 128, torch.float16), (3, 16, 2, 130, 64, torch.bfloat16)])
+def test_append_launch_matches_rotary_kernel_then_attention(B, H, KVH, S, D, dtype):
+    """b2d_gqa_decode_append (RoPE and the KV append inside the attention launch) gives the numbers of
+    b2d_rope_kv_append followed by the attention launch bit for bit: the output, both caches and the
+    lengths, for positions from 0 to S - 1 (and one outside the cache, which yields length 0)."""
+    from b200kernels.decode_attention import decode_attention_append
+    from b200kernels.glue import rope_kv_append
+    g = torch.Generator().manual_seed(S + B)
+    q = torch.randn(B, H * D, generator=g).to(dtype).to(DEV)
+    k = torch.randn(B, KVH * D, generator=g).to(dtype).to(DEV)
+    v = torch.randn(B, KVH * D, generator=g).to(dtype).to(DEV)
+    kc = torch.randn(B, KVH, S, D, generator=g).to(dtype).to(DEV)
+    vc = torch.randn(B, KVH, S, D, generator=g).to(dtype).to(DEV)
+    pos = torch.randint(0, S, (B,), generator=g)
+    pos[0], pos[-1] = 0, S - 1
+    if B > 2:
+        pos[1] = S   # outside the cache: length 0, nothing appended
+    pos = pos.to(DEV)
+    ang = torch.arange(S, dtype=torch.float32).view(-1, 1) * (1e-2 * torch.arange(D // 2, dtype=torch.float32) + 0.01)
+    cos = torch.cat([ang.cos(), ang.cos()], 1).to(dtype).to(DEV)
+    sin = torch.cat([ang.sin(), ang.sin()], 1).to(dtype).to(DEV)
+    # path 1: the rotary kernel, then the attention launch
+    kc1, vc1, q1 = kc.clone(), vc.clone(), q.clone()
+    sl1 = torch.zeros(B, dtype=torch.int32, device=DEV)
+    rope_kv_append(q1, k, v, pos, cos, sin, q1.view(B, H, D), kc1, vc1, sl1)
+    out1 = decode_attention(q1.view(B, H, 1, D), kc1, vc1, D ** -0.5, seqlens=sl1)
+    # path 2: one launch
+    kc2, vc2 = kc.clone(), vc.clone()
+    sl2 = torch.full((B,), -7, dtype=torch.int32, device=DEV)
+    out2 = torch.full((B, 1, H, D), float("nan"), dtype=dtype, device=DEV)
+    decode_attention_append(q, k, v, pos, cos, sin, kc2, vc2, D ** -0.5, sl2, out2)
+    torch.cuda.synchronize()
+    assert torch.equal(sl1, sl2)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    assert torch.equal(out1, out2)
