@@ -508,10 +508,11 @@ def run_b200(args):
     achieved = alg / (us * 1e-6) / 1e9
 
     # ---- our kernel launches per step: per layer 2 add+RMSNorm, RoPE + KV append (inside the attention
-    # partial launch when the engine folds it in), attention partial + combine and the NF4 launches (q/k/v,
+    # partial launch when the engine folds it in), attention partial + combine (one launch with
+    # B2D_ATTN_COMBINE=fused) and the NF4 launches (q/k/v,
     # o, gate/up, down at B <= 8; else 7 NF4 launches and SiLU*mul), plus the all-reduces under TP; plus the
     # final add+RMSNorm
-    glue = 4 if eng.attn_append else 5
+    glue = (3 if eng.attn_flags & L.ATTN_FUSED_COMBINE else 4) if eng.attn_append else 5
     per_layer = (glue + 4) if eng.pair else (glue + 7 + 1)
     if tp is not None and not eng.ar_fused:   # fused: the GEMMs push, the add+RMSNorm launches sum
         per_layer += 2

@@ -171,6 +171,8 @@ class DecodeEngine:
         # the streaming attention kernel also applies RoPE and appends the step's K/V (one launch fewer per
         # layer); B2D_ATTN_KERNEL=reg selects the separate rotary kernel + register-prefetch attention
         self.attn_append = os.environ.get("B2D_ATTN_KERNEL", "stream") != "reg"
+        # B2D_ATTN_COMBINE=fused: the append launch's last split CTA combines (no combine launch)
+        self.attn_flags = PDL | (_lib.ATTN_FUSED_COMBINE if os.environ.get("B2D_ATTN_COMBINE") == "fused" else 0)
         # rotary tables for every cache position, computed by the model's own rotary module
         pos = torch.arange(self.S, device=dev).view(1, -1)
         cos, sin = self.model.model.rotary_emb(self.r.view(B, 1, hid)[:1], pos)
@@ -200,7 +202,7 @@ class DecodeEngine:
                 w["q"].matmul(self.xn, out=self.q); w["k"].matmul(self.xn, out=self.k); w["v"].matmul(self.xn, out=self.v)
             if self.attn_append:   # RoPE + KV append inside the attention launch
                 decode_attention_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, self.k_cache[i],
-                                        self.v_cache[i], self.scale, self.seqlens, self.attn, flags=PDL)
+                                        self.v_cache[i], self.scale, self.seqlens, self.attn, flags=self.attn_flags)
             else:
                 q3 = self.q.view(B, H, D)
                 rope_kv_append(self.q, self.k, self.v, self.pos, self.cos, self.sin, q3, self.k_cache[i],

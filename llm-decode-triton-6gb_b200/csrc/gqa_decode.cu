@@ -117,6 +117,40 @@ __device__ __forceinline__ int o_chunk(int row, int c) {
   }
 }
 
+// Single-launch mode (both partial kernels): after a split CTA has written its partial, the last of the
+// sequence's valid splits to arrive combines them. The barrier orders every thread's partial stores
+// before thread 0's release; thread 0's acquire (and the barrier after it) orders the reads below after
+// every other split's partial. The counter returns to zero for the next launch.
+template <typename T, int D>
+__device__ __forceinline__ void last_split_combine(const AttnArgs& a, int b, int kvh, int len) {
+  __shared__ int s_last;
+  const int nvalid = min(a.nsplit, (len + a.chunk - 1) / a.chunk);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = a.counters + b * a.KVH + kvh;
+    const int last = atomic_add_acq_rel_gpu(ctr, 1) == nvalid - 1;
+    if (last) *ctr = 0;   // every split has arrived: reset for the next launch
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int64_t head0 = static_cast<int64_t>(b) * a.H + kvh * a.G;
+  for (int idx = threadIdx.x; idx < a.G * D; idx += kAttnWarps * 32) {
+    const int row = idx / D, d = idx - row * D;
+    const int64_t base = (head0 + row) * a.nsplit;
+    float mx = -INFINITY;
+    for (int i = 0; i < nvalid; ++i) mx = fmaxf(mx, __ldcg(a.ml + (base + i) * 2));
+    float num = 0.f, den = 0.f;
+    for (int i = 0; i < nvalid; ++i) {
+      const float m = __ldcg(a.ml + (base + i) * 2);
+      const float w = m == -INFINITY ? 0.f : exp2f(m - mx);
+      num += w * __ldcg(a.acc + (base + i) * D + d);
+      den += w * __ldcg(a.ml + (base + i) * 2 + 1);
+    }
+    store_out<T>(a, b, kvh * a.G + row, d, den > 0.f ? num / den : 0.f);
+  }
+}
+
 template <typename T, int D, bool TWO_HALVES>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const AttnArgs a) {
   constexpr int KSTEPS = D / 16;   // MMA k-steps over the head dim
@@ -286,37 +320,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_partial_kernel(const A
     }
   }
   pdl_launch_dependents();
-  if (!a.fused) return;
-
-  // ---- single-launch mode: the last of the sequence's valid splits to arrive combines them. The
-  // barrier orders every thread's partial stores before thread 0's release; thread 0's acquire (and
-  // the barrier after it) orders the reads below after every other split's partial.
-  __shared__ int s_last;
-  const int nvalid = min(a.nsplit, (len + a.chunk - 1) / a.chunk);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int* ctr = a.counters + b * a.KVH + kvh;
-    const int last = atomic_add_acq_rel_gpu(ctr, 1) == nvalid - 1;
-    if (last) *ctr = 0;   // every split has arrived: reset for the next launch
-    s_last = last;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  const int64_t head0 = static_cast<int64_t>(b) * a.H + kvh * a.G;
-  for (int idx = threadIdx.x; idx < a.G * D; idx += kAttnWarps * 32) {
-    const int row = idx / D, d = idx - row * D;
-    const int64_t base = (head0 + row) * a.nsplit;
-    float mx = -INFINITY;
-    for (int i = 0; i < nvalid; ++i) mx = fmaxf(mx, __ldcg(a.ml + (base + i) * 2));
-    float num = 0.f, den = 0.f;
-    for (int i = 0; i < nvalid; ++i) {
-      const float m = __ldcg(a.ml + (base + i) * 2);
-      const float w = m == -INFINITY ? 0.f : exp2f(m - mx);
-      num += w * __ldcg(a.acc + (base + i) * D + d);
-      den += w * __ldcg(a.ml + (base + i) * 2 + 1);
-    }
-    store_out<T>(a, b, kvh * a.G + row, d, den > 0.f ? num / den : 0.f);
-  }
+  if (a.fused) last_split_combine<T, D>(a, b, kvh, len);
 }
 
 // One CTA per (b, h), one thread per head-dim element. OT: output dtype.
@@ -474,6 +478,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
   if (a.append && split == 0 && kvh == 0 && tid == 0) a.seqlens_out[b] = len;
   if (t_begin >= len) {   // this split holds no keys; the combine skips it
     cp_async_wait<0>();
+    if (a.fused && split == 0)   // an empty sequence: its heads get zeros, as the combine kernel writes
+      for (int idx = tid; idx < a.G * D; idx += kAttnWarps * 32) store_out<T>(a, b, kvh * a.G + idx / D, idx % D, 0.f);
     return;
   }
   const int t_end = min(t_begin + a.chunk, len);
@@ -667,6 +673,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
     }
   }
   pdl_launch_dependents();
+  if (a.fused) last_split_combine<T, D>(a, b, kvh, len);
 }
 
 int check_attn(int B, int H, int KVH, int S, int D, int dtype) {
@@ -707,8 +714,7 @@ int launch_partial_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 // Which partial kernel serves a two-kernel launch: B2D_ATTN_KERNEL=stream / reg in the environment selects
 // the streaming or the register-prefetch kernel (read at every call, for comparisons); otherwise
-// kStreamByDefault decides. Single-launch combines always run the register-prefetch kernel, which
-// implements them.
+// kStreamByDefault decides. Both kernels implement the single-launch combine.
 constexpr bool kStreamByDefault = true;   // measured faster at every shape (B = 1, 8; S = 512 .. 32768)
 bool stream_attn_enabled() {
   const char* v = std::getenv("B2D_ATTN_KERNEL");
@@ -738,7 +744,7 @@ int launch_stream_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
 }
 
 int launch_partial(const AttnArgs& a, int D, int dtype, cudaStream_t s, bool pdl = false) {
-  if (!a.fused && stream_attn_enabled()) {
+  if (stream_attn_enabled()) {
     if (dtype == B2D_F16) return D == 64 ? launch_stream_t<__half, 64>(a, s, pdl) : launch_stream_t<__half, 128>(a, s, pdl);
     return D == 64 ? launch_stream_t<__nv_bfloat16, 64>(a, s, pdl) : launch_stream_t<__nv_bfloat16, 128>(a, s, pdl);
   }
@@ -951,13 +957,17 @@ extern "C" int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_n
   a.pos = pos;
   a.rcos = rcos; a.rsin = rsin; a.ld_cs = ld_cs;
   a.seqlens_out = seqlens;
+  if ((flags & B2D_ATTN_FUSED_COMBINE) && nsplit <= kMaxFusedSplits && B * KVH <= kMaxAttnCounters) {
+    a.fused = 1;
+    a.out_f32 = out_dtype == B2D_F32;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
   if (dtype == B2D_F16)
     st = D == 64 ? launch_stream_t<__half, 64>(a, s, pdl) : launch_stream_t<__half, 128>(a, s, pdl);
   else
     st = D == 64 ? launch_stream_t<__nv_bfloat16, 64>(a, s, pdl) : launch_stream_t<__nv_bfloat16, 128>(a, s, pdl);
-  if (st != B2D_OK) return st;
+  if (st != B2D_OK || a.fused) return st;
   return launch_combine(a, D, out_dtype, s, true);
 }
 

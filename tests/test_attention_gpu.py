@@ -142,11 +142,12 @@ def test_rejects_bad_inputs():
 
 @pytest.mark.parametrize("B,H,KVH,S,D", [(8, 32, 8, 320, 128), (3, 64, 4, 1000, 64), (2, 32, 8, 4096, 128)])
 @pytest.mark.parametrize("odt", [torch.float16, torch.float32])
-def test_single_launch_combine_matches_two_kernels(B, H, KVH, S, D, odt, monkeypatch):
-    """B2D_ATTN_FUSED_COMBINE (the last split CTA of the register-prefetch kernel combines) gives the
-    two-kernel result of the same partial kernel bit for bit, including empty and ragged sequences, and
-    leaves the workspace counters at zero."""
-    monkeypatch.setenv("B2D_ATTN_KERNEL", "reg")
+@pytest.mark.parametrize("kernel", ["reg", "stream"])
+def test_single_launch_combine_matches_two_kernels(B, H, KVH, S, D, odt, kernel, monkeypatch):
+    """B2D_ATTN_FUSED_COMBINE (the last split CTA of the partial kernel combines) gives the two-kernel
+    result of the same partial kernel bit for bit, for both partial kernels, including empty and ragged
+    sequences, and leaves the workspace counters at zero."""
+    monkeypatch.setenv("B2D_ATTN_KERNEL", kernel)
     g = torch.Generator().manual_seed(S + B)
     q = torch.randn(B, H, 1, D, generator=g).half().to(DEV)
     k = torch.randn(B, KVH, S, D, generator=g).half().to(DEV)
@@ -218,7 +219,8 @@ def test_static_prefix_flag_matches_oracle():
 def test_append_launch_matches_rotary_kernel_then_attention(B, H, KVH, S, D, dtype):
     """b2d_gqa_decode_append (RoPE and the KV append inside the attention launch) gives the numbers of
     b2d_rope_kv_append followed by the attention launch bit for bit: the output, both caches and the
-    lengths, for positions from 0 to S - 1 (and one outside the cache, which yields length 0)."""
+    lengths, for positions from 0 to S - 1 (and one outside the cache, which yields length 0); so does
+    the append launch with the single-launch combine, on two calls in a row."""
     from b200kernels.decode_attention import decode_attention_append
     from b200kernels.glue import rope_kv_append
     g = torch.Generator().manual_seed(S + B)
@@ -245,7 +247,17 @@ def test_append_launch_matches_rotary_kernel_then_attention(B, H, KVH, S, D, dty
     sl2 = torch.full((B,), -7, dtype=torch.int32, device=DEV)
     out2 = torch.full((B, 1, H, D), float("nan"), dtype=dtype, device=DEV)
     decode_attention_append(q, k, v, pos, cos, sin, kc2, vc2, D ** -0.5, sl2, out2)
+    # path 3: one launch with the single-launch combine, twice (the arrival counters return to zero)
+    kc3, vc3 = kc.clone(), vc.clone()
+    sl3 = torch.full((B,), -7, dtype=torch.int32, device=DEV)
+    outs3 = []
+    for _ in range(2):
+        outs3.append(torch.full((B, 1, H, D), float("nan"), dtype=dtype, device=DEV))
+        decode_attention_append(q, k, v, pos, cos, sin, kc3, vc3, D ** -0.5, sl3, outs3[-1],
+                                flags=_lib.ATTN_FUSED_COMBINE | _lib.LAUNCH_PDL)
     torch.cuda.synchronize()
-    assert torch.equal(sl1, sl2)
+    assert torch.equal(sl1, sl2) and torch.equal(sl1, sl3)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    assert torch.equal(kc1, kc3) and torch.equal(vc1, vc3)
     assert torch.equal(out1, out2)
+    assert torch.equal(outs3[0], out2) and torch.equal(outs3[1], out2)
