@@ -172,7 +172,7 @@ class DecodeEngine:
         # layer); B2D_ATTN_KERNEL=reg selects the separate rotary kernel + register-prefetch attention
         self.attn_append = os.environ.get("B2D_ATTN_KERNEL", "stream") != "reg"
         # B2D_ATTN_COMBINE=fused: the append launch's last split CTA combines (no combine launch)
-        self.attn_flags = PDL | (_lib.ATTN_FUSED_COMBINE if os.environ.get("B2D_ATTN_COMBINE") == "fused" else 0)
+        self.attn_flags = _lib.LAUNCH_PDL | (_lib.ATTN_FUSED_COMBINE if os.environ.get("B2D_ATTN_COMBINE") == "fused" else 0)
         # rotary tables for every cache position, computed by the model's own rotary module
         pos = torch.arange(self.S, device=dev).view(1, -1)
         cos, sin = self.model.model.rotary_emb(self.r.view(B, 1, hid)[:1], pos)
