@@ -255,6 +255,13 @@ int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_new, int64_t
                           void* workspace, size_t workspace_bytes,
                           void* out, int64_t so_b, int64_t so_h, int out_dtype, int flags, void* stream);
 
+/* One-shot L2 prefetch hint (no counterpart in the reference): the next b2d_gqa_decode_append call made by
+ * this host thread also prefetches up to 4 device ranges into L2 (ptrs 16-byte aligned; the whole 16-byte
+ * units of each range), spread over its CTAs and issued before any dependency wait, then the hint is
+ * cleared. Meant for static data the launches after it read (the next GEMMs' weights); no result
+ * depends on it. */
+int b2d_l2_prefetch_hint(const void* const* ptrs, const int64_t* bytes, int n);
+
 /* ================================================================ decode-step glue
  * The small per-layer operations of a Mistral decoder layer around the two hot paths, as kernels
  * that take B2D_LAUNCH_PDL (no counterpart in the reference, which runs these as separate torch ops:

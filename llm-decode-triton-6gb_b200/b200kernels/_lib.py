@@ -65,6 +65,7 @@ SIGNATURES = {
                                      _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p,
                                      _i32, _i32, _i32, _i32, _i32, _f32, _i32, _p, _sz,
                                      _p, _i64, _i64, _i32, _i32, _p]),
+    "b2d_l2_prefetch_hint": (_i32, [_p, _p, _i32]),
     "b2d_add_rmsnorm": (_i32, [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i32, _i32, _i32, _i32, _p]),
     "b2d_rope_kv_append": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64,
                                   _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p,

@@ -89,6 +89,16 @@ def decode_attention(q, k, v, scale=None, chunk=None, block_s=None, seqlens=None
     return out
 
 
+def l2_prefetch_hint(tensors) -> None:
+    """The next ``decode_attention_append`` call on this thread also prefetches these device tensors'
+    bytes into L2 (at most 4; static data that later launches read, e.g. the next GEMMs' weights)."""
+    import ctypes
+    n = len(tensors)
+    ptrs = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in tensors])
+    nbytes = (ctypes.c_int64 * max(n, 1))(*[t.numel() * t.element_size() for t in tensors])
+    _lib.call("b2d_l2_prefetch_hint", ctypes.addressof(ptrs), ctypes.addressof(nbytes), n)
+
+
 def decode_attention_append(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos: torch.Tensor,
                             cos: torch.Tensor, sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                             scale: float, seqlens: torch.Tensor, out: torch.Tensor, flags: int = 0) -> torch.Tensor:

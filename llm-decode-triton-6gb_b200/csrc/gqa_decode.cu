@@ -38,6 +38,8 @@ constexpr size_t kAttnCounterBytes = 64 * 1024;
 constexpr int kMaxAttnCounters = static_cast<int>(kAttnCounterBytes / 4);
 constexpr int kMaxFusedSplits = 64;   // the in-kernel combine loops over the splits per element
 
+constexpr int kMaxL2Prefetch = 4;
+
 struct AttnArgs {
   const void* q; int64_t sq_b, sq_h;
   const void* k; int64_t sk_b, sk_h, sk_s;
@@ -61,6 +63,11 @@ struct AttnArgs {
   const int64_t* pos;
   const void* rcos; const void* rsin; int64_t ld_cs;
   int32_t* seqlens_out;
+  // L2 prefetch of static data the following launches read (the next GEMMs' weights): the CTAs issue
+  // bulk L2 prefetches of equal slices of each range before any dependency wait; no result depends on it
+  int npf;
+  const char* pf_base[kMaxL2Prefetch];
+  int64_t pf_bytes[kMaxL2Prefetch];   // multiples of 16
 };
 
 template <typename T>
@@ -411,6 +418,21 @@ constexpr size_t stream_smem_bytes() {
   return static_cast<size_t>(kStreamStages) * 2 * kStreamKeys * D * 2;
 }
 
+// This CTA's share of the launch's L2 prefetch ranges: slice `cta` of each range (16-byte multiples), in
+// bulk prefetches of at most 64 KB. One thread issues them; they complete on their own.
+__device__ __forceinline__ void l2_prefetch_slices(const AttnArgs& a) {
+  const int64_t ncta = static_cast<int64_t>(gridDim.x) * gridDim.y * gridDim.z;
+  const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
+  for (int r = 0; r < a.npf && r < kMaxL2Prefetch; ++r) {
+    const int64_t per = ((a.pf_bytes[r] + ncta - 1) / ncta + 15) & ~static_cast<int64_t>(15);
+    const int64_t end = min(a.pf_bytes[r], (cta + 1) * per);
+    for (int64_t o = cta * per; o < end; o += 65536) {
+      const uint32_t n = static_cast<uint32_t>(end - o < 65536 ? end - o : 65536);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.pf_base[r] + o), "r"(n) : "memory");
+    }
+  }
+}
+
 template <typename T, int D, bool TWO_HALVES>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const AttnArgs a) {
   constexpr int KSTEPS = D / 16;        // MMA k-steps over the head dim (S = Q K^T)
@@ -430,6 +452,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) gqa_stream_kernel(const At
   const T* kbase = static_cast<const T*>(a.k) + b * a.sk_b + kvh * a.sk_h;
   const T* vbase = static_cast<const T*>(a.v) + b * a.sv_b + kvh * a.sv_h;
   const uint32_t sbase = smem_u32(smem);
+  if (a.npf > 0 && tid == 0) l2_prefetch_slices(a);
 
   // copies of stage `it` into buffer `bf` (every thread: 64 keys x CH chunks of K and of V); keys at or
   // past `lim` are zero-filled without a global read
@@ -921,6 +944,24 @@ extern "C" int b2d_gqa_decode(const void* q, int64_t sq_b, int64_t sq_h, const v
 // Decode-step attention with the step's RoPE and KV append folded in (no counterpart in the reference,
 // whose decode step rotates and appends with torch ops before calling its attention kernel). One launch of
 // the streaming partial kernel + the combine instead of the rotary/append kernel + both attention kernels.
+// One-shot L2 prefetch hint for this host thread's next b2d_gqa_decode_append call (then cleared).
+thread_local int t_npf = 0;
+thread_local const char* t_pf_base[kMaxL2Prefetch];
+thread_local int64_t t_pf_bytes[kMaxL2Prefetch];
+
+extern "C" int b2d_l2_prefetch_hint(const void* const* ptrs, const int64_t* bytes, int n) {
+  if (n < 0 || n > kMaxL2Prefetch || (n > 0 && (!ptrs || !bytes))) return B2D_ERR_ARG;
+  t_npf = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!ptrs[i] || bytes[i] < 0) return B2D_ERR_ARG;
+    if (!aligned(ptrs[i], 16)) return B2D_ERR_ALIGN;
+    t_pf_base[t_npf] = static_cast<const char*>(ptrs[i]);
+    t_pf_bytes[t_npf] = bytes[i] & ~static_cast<int64_t>(15);   // whole 16-byte units inside the range
+    ++t_npf;
+  }
+  return B2D_OK;
+}
+
 extern "C" int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_new, int64_t ldk, const void* v_new,
                                      int64_t ldv, const int64_t* pos, const void* rcos, const void* rsin,
                                      int64_t ld_cs, void* k_cache, int64_t sk_b, int64_t sk_h, int64_t sk_s,
@@ -961,6 +1002,9 @@ extern "C" int b2d_gqa_decode_append(const void* q, int64_t ldq, const void* k_n
     a.fused = 1;
     a.out_f32 = out_dtype == B2D_F32;
   }
+  a.npf = t_npf;
+  for (int i = 0; i < t_npf; ++i) { a.pf_base[i] = t_pf_base[i]; a.pf_bytes[i] = t_pf_bytes[i]; }
+  t_npf = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & B2D_LAUNCH_PDL) != 0;
   if (dtype == B2D_F16)

@@ -255,8 +255,17 @@ def test_append_launch_matches_rotary_kernel_then_attention(B, H, KVH, S, D, dty
         outs3.append(torch.full((B, 1, H, D), float("nan"), dtype=dtype, device=DEV))
         decode_attention_append(q, k, v, pos, cos, sin, kc3, vc3, D ** -0.5, sl3, outs3[-1],
                                 flags=_lib.ATTN_FUSED_COMBINE | _lib.LAUNCH_PDL)
+    # path 4: one launch that also prefetches unrelated static data into L2 (a hint: same numbers)
+    from b200kernels.decode_attention import l2_prefetch_hint
+    kc4, vc4 = kc.clone(), vc.clone()
+    sl4 = torch.full((B,), -7, dtype=torch.int32, device=DEV)
+    out4 = torch.full((B, 1, H, D), float("nan"), dtype=dtype, device=DEV)
+    junk = torch.randn(3 << 20, generator=g).to(DEV)
+    l2_prefetch_hint([junk, kc, vc[1:]])
+    decode_attention_append(q, k, v, pos, cos, sin, kc4, vc4, D ** -0.5, sl4, out4, flags=_lib.LAUNCH_PDL)
     torch.cuda.synchronize()
-    assert torch.equal(sl1, sl2) and torch.equal(sl1, sl3)
+    assert torch.equal(sl1, sl2) and torch.equal(sl1, sl3) and torch.equal(sl1, sl4)
+    assert torch.equal(kc1, kc4) and torch.equal(vc1, vc4) and torch.equal(out4, out2)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
     assert torch.equal(kc1, kc3) and torch.equal(vc1, vc3)
     assert torch.equal(out1, out2)

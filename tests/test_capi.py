@@ -112,3 +112,19 @@ def test_device_calls_fail_loudly_without_gpu():
     p = C.addressof(buf)
     st = lib.b2d_nf4_quantize(p, 64, 2, p, p, p, None)
     assert st == 7
+
+
+def test_l2_prefetch_hint_validation():
+    """The one-shot L2 hint is host-side only: its checks run without a GPU."""
+    lib = _lib.load()
+    buf = C.create_string_buffer(64 + 32)
+    base = (C.addressof(buf) + 15) & ~15
+    ptrs = (C.c_void_p * 5)(*([base] * 5))
+    nb = (C.c_int64 * 5)(*([64] * 5))
+    assert lib.b2d_l2_prefetch_hint(C.addressof(ptrs), C.addressof(nb), 0) == 0
+    assert lib.b2d_l2_prefetch_hint(C.addressof(ptrs), C.addressof(nb), 4) == 0
+    assert lib.b2d_l2_prefetch_hint(C.addressof(ptrs), C.addressof(nb), 5) == 1   # B2D_ERR_ARG
+    assert lib.b2d_l2_prefetch_hint(None, None, 1) == 1   # B2D_ERR_ARG
+    odd = (C.c_void_p * 1)(base + 8)
+    assert lib.b2d_l2_prefetch_hint(C.addressof(odd), C.addressof(nb), 1) == 4   # B2D_ERR_ALIGN
+    assert lib.b2d_l2_prefetch_hint(C.addressof(ptrs), C.addressof(nb), 0) == 0   # leaves no hint pending
